@@ -1,0 +1,246 @@
+"""Paged-KV decode wrapper shaped like FlashInfer's BatchDecodeWithPagedKVCacheWrapper.
+
+The reference decodes one request at a time through
+``single_decode_with_kv_cache_with_jit_module(mod, q, k, v, None, zhi8, ...)``
+(e2e_pipeline/atflash_e2e_fafi.py:106-110) with the window in the K-load
+predicate (kernels/flashinfer_port/decode.cuh.diff:51-89). This wrapper keeps
+FlashInfer's batch plan()/run() interface and adds ``window_table``.
+
+Window modes: "snap16" (16-dim levels at per-key granularity, equal to
+atflash/reference.py with phase="decode", block_m = block_n = 1) or "vec8"
+(8-dim slices, the FlashInfer port's table; sorted-pair K layout only).
+"""
+import ctypes
+import math
+from typing import Optional, Sequence, Tuple, Union
+
+import numpy as np
+import torch
+
+from . import _ffi, _runtime
+from .window_table import KERNEL_CAP, WindowTable, zhi_slice_vec8
+
+_LAYOUTS = {"sorted_pair": _ffi.ATF_LAYOUT_SORTED_PAIR, "rotate_half": _ffi.ATF_LAYOUT_ROTATE_HALF}
+
+
+def _host_i32(t) -> np.ndarray:
+    if isinstance(t, torch.Tensor):
+        return t.detach().to("cpu", torch.int32).numpy().astype(np.int32, copy=True)
+    return np.asarray(t, dtype=np.int32).copy()
+
+
+class BatchDecodeWithPagedKVCacheWrapper:
+    def __init__(self, float_workspace_buffer: torch.Tensor, kv_layout: str = "NHD",
+                 use_cuda_graph: bool = False, use_tensor_cores: bool = False,
+                 paged_kv_indptr_buffer=None, paged_kv_indices_buffer=None,
+                 paged_kv_last_page_len_buffer=None, backend: str = "auto", jit_args=None):
+        if kv_layout not in ("NHD", "HND"):
+            raise ValueError("kv_layout must be NHD or HND")
+        if not float_workspace_buffer.is_cuda:
+            raise ValueError("the workspace buffer must be a CUDA tensor")
+        self._ws = float_workspace_buffer
+        self._kv_layout = kv_layout
+        self._plan = None
+
+    @property
+    def is_cuda_graph_enabled(self) -> bool:
+        return False
+
+    def reset_workspace_buffer(self, float_workspace_buffer, int_workspace_buffer=None):
+        self._ws = float_workspace_buffer
+
+    def plan(self, indptr, indices, last_page_len, num_qo_heads: int, num_kv_heads: int,
+             head_dim: int, page_size: int, pos_encoding_mode: str = "NONE", window_left: int = -1,
+             logits_soft_cap=None, q_data_type="bfloat16", kv_data_type=None, data_type=None,
+             sm_scale: Optional[float] = None, rope_scale=None, rope_theta=None,
+             non_blocking: bool = True, *, window_table: Union[None, WindowTable, Sequence[int]] = None,
+             window_mode: str = "snap16", qk_layout: str = "sorted_pair",
+             max_chunk_keys: int = 0, min_chunk_keys: int = 0):
+        """Build the split-KV schedule for a batch of paged requests.
+
+        window_table: None (dense), a WindowTable, or a zhi level tuple (snap16).
+        qk_layout: pair order of the cached K and of q ("sorted_pair" or "rotate_half").
+        """
+        if pos_encoding_mode != "NONE":
+            raise NotImplementedError("RoPE is applied before the cache (pos_encoding_mode NONE)")
+        if window_left != -1 or logits_soft_cap not in (None, 0.0):
+            raise NotImplementedError("window_left / logits_soft_cap are not supported")
+        if head_dim != 128:
+            raise NotImplementedError("head_dim must be 128")
+        if window_mode not in ("snap16", "vec8"):
+            raise ValueError("window_mode must be snap16 or vec8")
+        if qk_layout not in _LAYOUTS:
+            raise ValueError(f"qk_layout must be one of {sorted(_LAYOUTS)}")
+        dev = self._ws.device
+        indptr_h = _host_i32(indptr)
+        lpl_h = _host_i32(last_page_len)
+        B = len(indptr_h) - 1
+        if B < 1 or len(lpl_h) != B:
+            raise ValueError("indptr must have batch+1 entries and last_page_len batch entries")
+        nnz = int(indptr_h[-1])
+        idx_dev = indices if isinstance(indices, torch.Tensor) else torch.tensor(indices)
+        if idx_dev.numel() < nnz:
+            raise ValueError("indices is shorter than indptr[-1]")
+        if np.any(np.diff(indptr_h) < 0) or indptr_h[0] != 0:
+            raise ValueError("indptr must start at 0 and be non-decreasing")
+        pp = _ffi.AtfDecodePlanParams()
+        pp.batch_size, pp.num_qo_heads, pp.num_kv_heads = B, num_qo_heads, num_kv_heads
+        pp.head_dim, pp.page_size = head_dim, page_size
+        pp.indptr_host = indptr_h.ctypes.data
+        pp.last_page_len_host = lpl_h.ctypes.data
+        pp.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        pp.min_chunk_keys, pp.max_chunk_keys = int(min_chunk_keys), int(max_chunk_keys)
+        plan = _ffi.AtfDecodePlan()
+        lib = _ffi.load()
+        _ffi.check("atf_decode_plan", lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)))
+        items = np.zeros((max(1, plan.num_items), 4), dtype=np.int32)
+        item_indptr = np.zeros(B + 1, dtype=np.int32)
+        _ffi.check("atf_decode_plan", lib.atf_decode_plan(
+            ctypes.byref(pp), items.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), items.shape[0],
+            item_indptr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(plan)))
+        need = 4 * (plan.partial_o_floats + plan.partial_lse_floats) + 256
+        if self._ws.numel() * self._ws.element_size() < need:
+            raise ValueError(f"workspace too small: need {need} bytes")
+        # window tables
+        zhi16 = [KERNEL_CAP] * 8
+        zhi8 = [2 ** 31 - 1] * 16
+        mode = _ffi.ATF_WINDOW_OFF
+        if window_table is not None:
+            if window_mode == "vec8":
+                if qk_layout != "sorted_pair":
+                    raise ValueError("vec8 windows need the sorted-pair K layout")
+                if not isinstance(window_table, WindowTable):
+                    zhi8 = [int(x) for x in window_table]
+                    if len(zhi8) != 16:
+                        raise ValueError("a vec8 table has 16 entries")
+                else:
+                    zhi8 = window_table.zhi8
+                mode = _ffi.ATF_WINDOW_VEC8
+            else:
+                zhi16 = list(window_table.zhi16 if isinstance(window_table, WindowTable)
+                             else [int(x) for x in window_table])
+                if len(zhi16) != 8:
+                    raise ValueError("a zhi level table has 8 entries")
+                zhi16[0] = max(zhi16[0], KERNEL_CAP)
+                mode = _ffi.ATF_WINDOW_SNAP16
+        kv_lens = [(int(indptr_h[b + 1] - indptr_h[b]) - 1) * page_size + int(lpl_h[b])
+                   if indptr_h[b + 1] > indptr_h[b] else 0 for b in range(B)]
+        self._plan = {
+            "B": B, "Hq": num_qo_heads, "Hkv": num_kv_heads, "page_size": page_size,
+            "num_items": plan.num_items, "chunk_keys": plan.chunk_keys,
+            "items": torch.from_numpy(items).to(dev, non_blocking=False),
+            "item_indptr": torch.from_numpy(item_indptr).to(dev),
+            "indptr": torch.from_numpy(indptr_h).to(dev),
+            "indices": idx_dev.to(device=dev, dtype=torch.int32).contiguous(),
+            "last_page_len": torch.from_numpy(lpl_h).to(dev),
+            "po_floats": plan.partial_o_floats, "pl_floats": plan.partial_lse_floats,
+            "sm_scale": float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(head_dim),
+            "window": mode, "zhi16": zhi16, "zhi8": zhi8, "layout": _LAYOUTS[qk_layout],
+            "kv_lens": kv_lens,
+        }
+
+    begin_forward = plan
+
+    def run(self, q: torch.Tensor, paged_kv_cache, *args, q_scale=None, k_scale=None, v_scale=None,
+            out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+            return_lse: bool = False, enable_pdl=None, window_left=None,
+            q_pos: Optional[torch.Tensor] = None, kv_pos0: Optional[torch.Tensor] = None,
+            out_dtype: Optional[torch.dtype] = None):
+        """q (B, Hq, 128) bf16; paged_kv_cache = (k_pages, v_pages) or one tensor with
+        a k/v axis at dim 1. Returns out (B, Hq, 128) [, lse (B, Hq), natural log]."""
+        if self._plan is None:
+            raise RuntimeError("plan() must be called before run()")
+        if q_scale is not None or k_scale is not None or v_scale is not None:
+            raise NotImplementedError("fp8 scales are not supported")
+        P = self._plan
+        if isinstance(paged_kv_cache, (tuple, list)):
+            kc, vc = paged_kv_cache
+        else:
+            kc, vc = paged_kv_cache[:, 0], paged_kv_cache[:, 1]
+        dev = _runtime.require_cuda(q, kc, vc)
+        if kc.dtype != torch.bfloat16 or vc.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
+            raise TypeError("q and the KV cache must be bfloat16")
+        if kc.stride() != vc.stride() or kc.shape != vc.shape or kc.dim() != 4:
+            raise ValueError("k and v pages must have the same 4-d shape and strides")
+        if kc.stride(-1) != 1 or q.stride(-1) != 1:
+            raise ValueError("the head_dim axis must be contiguous")
+        if self._kv_layout == "NHD":
+            _, page, hkv, d = kc.shape
+            s_page, s_tok, s_head = kc.stride(0), kc.stride(1), kc.stride(2)
+        else:
+            _, hkv, page, d = kc.shape
+            s_page, s_head, s_tok = kc.stride(0), kc.stride(1), kc.stride(2)
+        if page != P["page_size"] or hkv != P["Hkv"] or d != 128:
+            raise ValueError("KV cache shape does not match the plan")
+        B, Hq = P["B"], P["Hq"]
+        if tuple(q.shape) != (B, Hq, 128):
+            raise ValueError(f"q must be ({B}, {Hq}, 128)")
+        odt = out_dtype or (out.dtype if out is not None else torch.bfloat16)
+        if out is None:
+            out = torch.empty((B, Hq, 128), dtype=odt, device=dev)
+        if return_lse and lse is None:
+            lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
+        ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
+        base = (ws.data_ptr() + 255) // 256 * 256
+        po = base
+        pl = base + 4 * P["po_floats"]
+        a = _ffi.AtfDecodeParams()
+        a.q, a.q_stride_b, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
+        a.k_cache, a.v_cache = kc.data_ptr(), vc.data_ptr()
+        a.kv_stride_page, a.kv_stride_token, a.kv_stride_head = s_page, s_tok, s_head
+        a.kv_layout = _ffi.ATF_KV_NHD if self._kv_layout == "NHD" else _ffi.ATF_KV_HND
+        a.qk_layout = P["layout"]
+        a.indptr, a.indices = P["indptr"].data_ptr(), P["indices"].data_ptr()
+        a.last_page_len = P["last_page_len"].data_ptr()
+        a.items, a.item_indptr, a.num_items = P["items"].data_ptr(), P["item_indptr"].data_ptr(), P["num_items"]
+        a.batch_size, a.num_qo_heads, a.num_kv_heads, a.head_dim, a.page_size = B, Hq, P["Hkv"], 128, page
+        keep = []
+        if q_pos is not None:
+            q_pos = q_pos.to(device=dev, dtype=torch.int64).contiguous()
+            keep.append(q_pos)
+            a.q_pos = q_pos.data_ptr()
+        if kv_pos0 is not None:
+            kv_pos0 = kv_pos0.to(device=dev, dtype=torch.int64).contiguous()
+            keep.append(kv_pos0)
+            a.kv_pos0 = kv_pos0.data_ptr()
+        a.sm_scale = P["sm_scale"]
+        a.window = P["window"]
+        for i in range(8):
+            a.zhi16[i] = P["zhi16"][i]
+        for i in range(16):
+            a.zhi8[i] = P["zhi8"][i]
+        a.partial_o, a.partial_lse = po, pl
+        a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+        a.out_dtype = _ffi.ATF_DTYPE_F32 if out.dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
+        a.lse_out = lse.data_ptr() if lse is not None else None
+        a.error_flag = _runtime.error_flag(dev).data_ptr()
+        with torch.cuda.device(dev):
+            rc = _ffi.load().atf_decode_run(ctypes.byref(a), _runtime.stream_handle(dev))
+        _ffi.check("atf_decode_run", rc)
+        return (out, lse) if return_lse else out
+
+    forward = run
+
+
+def lse_merge(part_o: torch.Tensor, part_lse: torch.Tensor, *, lse_log2: bool = False,
+              out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False):
+    """Merge P partial states: part_o (P, B, H, 128) fp32, part_lse (P, B, H) fp32."""
+    dev = _runtime.require_cuda(part_o, part_lse)
+    Pn, B, H, D = part_o.shape
+    if D != 128 or tuple(part_lse.shape) != (Pn, B, H):
+        raise ValueError("part_o must be (P, B, H, 128) and part_lse (P, B, H)")
+    part_o = part_o.float().contiguous()
+    part_lse = part_lse.float().contiguous()
+    out = torch.empty((B, H, D), dtype=out_dtype, device=dev)
+    lse = torch.empty((B, H), dtype=torch.float32, device=dev) if return_lse else None
+    m = _ffi.AtfMergeParams()
+    m.part_o, m.part_lse, m.part_indptr = part_o.data_ptr(), part_lse.data_ptr(), None
+    m.num_parts, m.batch, m.num_heads, m.head_dim = Pn, B, H, D
+    m.lse_log2 = 1 if lse_log2 else 0
+    m.out, m.o_stride_b, m.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+    m.out_dtype = _ffi.ATF_DTYPE_F32 if out_dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
+    m.lse_out = lse.data_ptr() if lse is not None else None
+    with torch.cuda.device(dev):
+        rc = _ffi.load().atf_lse_merge(ctypes.byref(m), _runtime.stream_handle(dev))
+    _ffi.check("atf_lse_merge", rc)
+    return (out, lse) if return_lse else out

@@ -1,0 +1,139 @@
+"""Multi-GPU windowed attention: one process per GPU over torch.distributed.
+
+Prefill shards the *queries*: the sequence is cut into 2G blocks (G ranks) and
+rank i computes blocks i and 2G-1-i (zig-zag causal balance) against
+replicated K/V. Each block is a bottom-right-aligned chunk (q_offset = block
+start), so windows use global positions and, with block starts on the 128-row
+tile grid, every output row is bit-identical to the single-GPU run. There is no
+collective on this path (an optional all-gather of the output is separate).
+
+Decode shards the *KV sequence*: rank r holds keys [start_r, end_r) of every
+request in its own paged cache, runs the split-KV decode with global key
+positions (kv_pos0 = start_r) and the global query position, and returns a
+partial (O, LSE). One all-gather of (O fp32, LSE) over the group and an LSE merge
+give the result.
+
+The reference has no multi-GPU code (it is batch-1, single GPU); this module is
+the build's sharding of the same computation.
+"""
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+TILE = 128
+
+
+def zigzag_bounds(seqlen: int, world: int, align: int = TILE) -> List[int]:
+    """2*world+1 block boundaries, interior ones on multiples of `align`."""
+    nb = 2 * world
+    b = [0]
+    for i in range(1, nb):
+        x = int(round(i * seqlen / nb / align)) * align
+        b.append(min(max(x, b[-1]), seqlen))
+    b.append(seqlen)
+    return b
+
+
+def zigzag_blocks(seqlen: int, world: int, rank: int, align: int = TILE) -> List[Tuple[int, int]]:
+    """The two [start, end) query blocks of `rank`: blocks rank and 2*world-1-rank."""
+    b = zigzag_bounds(seqlen, world, align)
+    i, j = rank, 2 * world - 1 - rank
+    return [(b[i], b[i + 1]), (b[j], b[j + 1])]
+
+
+def causal_pairs(s: int, e: int) -> int:
+    """Query-key pairs of rows [s, e) under a causal mask (work of one block)."""
+    return (e * (e + 1) - s * (s + 1)) // 2
+
+
+def kv_shard_range(seqlen: int, world: int, rank: int, align: int = 1) -> Tuple[int, int]:
+    """Contiguous key range of `rank` when the KV sequence is split evenly."""
+    per = -(-seqlen // world)
+    per = -(-per // align) * align
+    return min(seqlen, rank * per), min(seqlen, (rank + 1) * per)
+
+
+def _rank_world(group) -> Tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=None,
+                    rank: Optional[int] = None, world: Optional[int] = None,
+                    window_table=None, causal: bool = True, softmax_scale=None,
+                    qk_layout: str = "sorted_pair", gather: bool = False,
+                    prefill_fn: Optional[Callable] = None):
+    """This rank's zig-zag share of a causal prefill over the full q/k/v.
+
+    Returns [(start, end, out_block)] for the rank's two blocks, or with
+    gather=True the full (B, S, Hq, D) output assembled by an all-gather."""
+    if prefill_fn is None:
+        from .prefill import prefill_fwd as prefill_fn
+    r0, w0 = _rank_world(group)
+    rank = r0 if rank is None else rank
+    world = w0 if world is None else world
+    S = q.shape[1]
+    if k.shape[1] != S:
+        raise ValueError("sharded prefill expects seqlen_q == seqlen_k")
+    outs = []
+    for (s, e) in zigzag_blocks(S, world, rank):
+        if e <= s:
+            outs.append((s, e, q.new_empty((q.shape[0], 0, q.shape[2], q.shape[3]))))
+            continue
+        o = prefill_fn(q[:, s:e], k[:, :e] if causal else k, v[:, :e] if causal else v,
+                       causal=causal, softmax_scale=softmax_scale, window_table=window_table,
+                       qk_layout=qk_layout, q_offset=s if causal else 0)
+        outs.append((s, e, o))
+    if not gather:
+        return outs
+    return gather_zigzag(outs, S, world, group)
+
+
+def gather_zigzag(outs, seqlen: int, world: int, group=None) -> torch.Tensor:
+    """All-gather every rank's two blocks into the full output (rows in order)."""
+    bounds = zigzag_bounds(seqlen, world)
+    maxlen = max(bounds[i + 1] - bounds[i] for i in range(2 * world))
+    ref = outs[0][2]
+    B, _, H, D = ref.shape
+    send = ref.new_zeros((2, B, maxlen, H, D))
+    for t, (s, e, o) in enumerate(outs):
+        send[t, :, : e - s] = o
+    recv = ref.new_empty((world, 2, B, maxlen, H, D))
+    dist.all_gather_into_tensor(recv.view(-1), send.view(-1), group=group)
+    full = ref.new_empty((B, seqlen, H, D))
+    for r in range(world):
+        for t, (s, e) in enumerate(zigzag_blocks(seqlen, world, r)):
+            full[:, s:e] = recv[r, t, :, : e - s]
+    return full
+
+
+def merge_partials(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
+                   merge_fn: Optional[Callable] = None, out_dtype=torch.bfloat16):
+    """All-gather per-rank partial states (O fp32 (B,H,D), LSE natural (B,H)) and
+    merge them: LSE = log sum exp LSE_r, O = sum exp(LSE_r - LSE) O_r."""
+    _, world = _rank_world(group)
+    B, H, D = o_local.shape
+    pack = torch.cat([o_local.float().reshape(B * H, D), lse_local.float().reshape(B * H, 1)], dim=1)
+    allp = pack.new_empty((world,) + tuple(pack.shape))
+    if world > 1:
+        dist.all_gather_into_tensor(allp.view(-1), pack.contiguous().view(-1), group=group)
+    else:
+        allp[0] = pack
+    po = allp[:, :, :D].reshape(world, B, H, D)
+    pl = allp[:, :, D].reshape(world, B, H)
+    if merge_fn is None:
+        from .decode import lse_merge
+        return lse_merge(po, pl, lse_log2=False, out_dtype=out_dtype, return_lse=True)
+    return merge_fn(po, pl)
+
+
+def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
+                   kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16):
+    """Decode with this rank's KV shard; `wrapper` is planned over the rank's local
+    pages. q_pos: global query position per request; kv_pos0: global position of
+    this rank's first key per request. Returns (out, lse) merged over the group."""
+    o, lse = wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                         out_dtype=torch.float32)
+    return merge_partials(o, lse, group=group, out_dtype=out_dtype)

@@ -1,0 +1,604 @@
+// Windowed paged-KV GQA decode (split-KV) and the log-sum-exp merge.
+//
+// Functional spec: the FlashInfer decode window port of the reference
+// (kernels/flashinfer_port/decode.cuh.diff): key rows outside a level's window
+// are excluded from the K load predicate (:63-69, :82-89) and from the QK dot
+// product (:28-37); the softmax still runs over every key; split-KV partials
+// are merged by their LSE. Here the decode is batched over requests and reads
+// a paged KV cache.
+//
+// CTA = (work item = request b and key range, kv head). 4 warps. Keys stream
+// through shared memory in 64-key stages (3 in flight) with 16-byte cp.async
+// loads; every 16-byte chunk of K whose level is outside the key's window is
+// zero-filled instead of read. Each warp owns 16 keys of a stage:
+//   S = Q K^T   mma.sync m16n8k16, rows = the G query heads of the group
+//               (padded to 16), one K-step per active 16-dim level;
+//   online softmax (log2 domain) per head;
+//   O += P V    mma.sync m16n8k16 over the 16 keys, 16 n-tiles of 8 dims.
+// The 4 warps merge their states through shared memory and write the item's
+// partial (O normalised, LSE log2); the merge kernel combines the items of a
+// request.
+//
+// Window at per-key granularity (block_n = 1 in atflash/reference.py): the key
+// at global position p has distance z = q_pos - p and reads L(z) levels,
+// L(z) = max(1, #{i : zhi16[i] >= z}); in vec8 mode (sorted-pair layout only)
+// 8-dim slice c is read iff z <= zhi8[c] (kernels/flashinfer_port/fiwin_common.py:35-46).
+#include <math.h>
+
+#include "atf_internal.h"
+
+namespace atf {
+namespace decode {
+
+constexpr int KEYS_PER_STAGE = 64;
+constexpr int NSTAGE = 3;
+constexpr int THREADS = 128;
+constexpr int ROW_BYTES = 256;  // 128 bf16
+constexpr int STAGE_BYTES = 2 * KEYS_PER_STAGE * ROW_BYTES;  // K then V
+constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES;             // 96 KB
+
+struct Args {
+  const __nv_bfloat16* q;
+  long long q_sb, q_sh;
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  long long s_page, s_tok, s_head;
+  const int* indptr;
+  const int* indices;
+  const int* last_page_len;
+  const int* items;
+  const int64_t* q_pos;
+  const int64_t* kv_pos0;
+  int Hq, Hkv, G, page_size;
+  float scale_log2;
+  int window, layout;
+  int zhi16[ATF_MAX_LEVELS];
+  int zhi8[ATF_MAX_SLICES];
+  float* part_o;
+  float* part_lse;
+};
+
+// 16-byte chunk (0..15) of a 128-dim row that holds half `hh` of level `i`.
+__device__ __forceinline__ int chunk_of(int layout, int i, int hh) {
+  return layout == ATF_LAYOUT_SORTED_PAIR ? 2 * i + hh : 8 * hh + (7 - i);
+}
+// Level (0..7) of chunk c.
+__device__ __forceinline__ int level_of_chunk(int layout, int c) {
+  return layout == ATF_LAYOUT_SORTED_PAIR ? (c >> 1) : 7 - (c & 7);
+}
+
+__device__ __forceinline__ int levels_at(const Args& a, long long z) {
+  if (a.window == ATF_WINDOW_OFF) return 8;
+  if (a.window == ATF_WINDOW_SNAP16) {
+    int L = 0;
+#pragma unroll
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi16[i]) >= z) ? 1 : 0;
+    return L < 1 ? 1 : L;
+  }
+  // vec8: a level is needed when its first (wider) slice is active.
+  int L = 0;
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi8[2 * i]) >= z) ? 1 : 0;
+  return L;
+}
+
+__device__ __forceinline__ bool chunk_active(const Args& a, int c, long long z) {
+  if (a.window == ATF_WINDOW_OFF) return true;
+  if (a.window == ATF_WINDOW_SNAP16) return level_of_chunk(a.layout, c) < levels_at(a, z);
+  return static_cast<long long>(a.zhi8[c]) >= z;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of (key row, logical 16-B chunk) inside a 64-row stage buffer;
+// the chunk index is XOR-swizzled with the row so that ldmatrix reads of 8
+// consecutive rows hit 8 distinct bank groups.
+__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
+  return static_cast<uint32_t>(row * ROW_BYTES + ((chunk ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.x, hk = blockIdx.y;
+  const int b = a.items[4 * item + 0];
+  const int k_beg = a.items[4 * item + 1];
+  const int k_end = a.items[4 * item + 2];
+  const int pg0 = a.indptr[b];
+  const int npages = a.indptr[b + 1] - pg0;
+  const long long kv_len =
+      npages > 0 ? static_cast<long long>(npages - 1) * a.page_size + a.last_page_len[b] : 0;
+  const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
+  const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+  const int G = a.G;
+  const int hq0 = hk * G;
+
+  // Q fragments (A operand): rows = heads g / g+8 of the group, K = the 16 dims
+  // of each level (first 8 from half 0, next 8 from half 1 of the level).
+  const int g = lane >> 2, t4 = lane & 3;
+  uint32_t qa[8][4];
+  {
+    const __nv_bfloat16* qrow0 = a.q + static_cast<long long>(b) * a.q_sb + static_cast<long long>(hq0 + g) * a.q_sh;
+    const __nv_bfloat16* qrow1 = qrow0 + 8 * a.q_sh;
+    const bool v0 = g < G, v1 = g + 8 < G;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c0 = chunk_of(a.layout, i, 0) * 8 + 2 * t4;
+      const int c1 = chunk_of(a.layout, i, 1) * 8 + 2 * t4;
+      qa[i][0] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0) : 0u;
+      qa[i][1] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0) : 0u;
+      qa[i][2] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c1) : 0u;
+      qa[i][3] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c1) : 0u;
+    }
+  }
+
+  const int nkeys = k_end - k_beg;
+  const int nst = (nkeys + KEYS_PER_STAGE - 1) / KEYS_PER_STAGE;
+
+  // Loader mapping: thread covers chunk (tid & 15) of rows (tid >> 4) + 8m.
+  auto issue_stage = [&](int s) {
+    const int buf = s % NSTAGE;
+    const uint32_t kb = sbase + buf * STAGE_BYTES;
+    const uint32_t vb = kb + KEYS_PER_STAGE * ROW_BYTES;
+    const int c = tid & 15;
+#pragma unroll
+    for (int m = 0; m < KEYS_PER_STAGE / 8; ++m) {
+      const int row = (tid >> 4) + 8 * m;
+      const int n = k_beg + s * KEYS_PER_STAGE + row;  // local key index of the request
+      const bool valid = n < k_end;
+      const int nn = valid ? n : k_end - 1;
+      const int page = a.indices[pg0 + nn / a.page_size];
+      const long long off = static_cast<long long>(page) * a.s_page +
+                            static_cast<long long>(nn % a.page_size) * a.s_tok +
+                            static_cast<long long>(hk) * a.s_head + c * 8;
+      const long long z = q_pos - (pos0 + n);
+      cp_async16(kb + sw_off(row, c), a.kc + off, valid && chunk_active(a, c, z));
+      cp_async16(vb + sw_off(row, c), a.vc + off, valid);
+    }
+  };
+
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+#pragma unroll
+  for (int s = 0; s < NSTAGE - 1; ++s) {
+    if (s < nst) issue_stage(s);
+    cp_async_commit();
+  }
+
+  for (int s = 0; s < nst; ++s) {
+    cp_async_wait<NSTAGE - 2>();
+    __syncthreads();
+    if (s + NSTAGE - 1 < nst) issue_stage(s + NSTAGE - 1);
+    cp_async_commit();
+
+    const int buf = s % NSTAGE;
+    const uint32_t kb = sbase + buf * STAGE_BYTES;
+    const uint32_t vb = kb + KEYS_PER_STAGE * ROW_BYTES;
+    const int key0 = k_beg + s * KEYS_PER_STAGE + warp * 16;  // first key of this warp
+    if (key0 < k_end) {
+      const int last = (key0 + 15 < k_end ? key0 + 15 : k_end - 1);
+      const int Lmax = levels_at(a, q_pos - (pos0 + last));
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      // ldmatrix lane roles: matrix mi = lane >> 3 (0: keys 0-7 half 0, 1: keys 0-7 half 1,
+      // 2: keys 8-15 half 0, 3: keys 8-15 half 1), row = lane & 7.
+      const int mi = lane >> 3;
+      const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < Lmax) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kb + sw_off(lrow, chunk_of(a.layout, i, mi & 1)), b0, b1, b2, b3);
+          mma16816(sc[0], qa[i], b0, b1);
+          mma16816(sc[1], qa[i], b2, b3);
+        }
+      }
+      // scores -> log2 domain, mask keys past the item end
+      float mloc[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
+          const float v = key < k_end ? sc[nt][e] * a.scale_log2 : -INFINITY;
+          sc[nt][e] = v;
+          mloc[e >> 1] = fmaxf(mloc[e >> 1], v);
+        }
+      float alpha[2], psum[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(0xffffffffu, mloc[r], 1));
+        mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(0xffffffffu, mloc[r], 2));
+        const float mnew = fmaxf(m_run[r], mloc[r]);
+        alpha[r] = (m_run[r] == -INFINITY) ? 0.f : ex2f(m_run[r] - mnew);
+        m_run[r] = mnew;
+        psum[r] = 0.f;
+      }
+      uint32_t pa[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const float p0 = ex2f(sc[nt][0] - m_run[0]);
+        const float p1 = ex2f(sc[nt][1] - m_run[0]);
+        const float p2 = ex2f(sc[nt][2] - m_run[1]);
+        const float p3 = ex2f(sc[nt][3] - m_run[1]);
+        psum[0] += p0 + p1;
+        psum[1] += p2 + p3;
+        pa[2 * nt + 0] = pack2(p0, p1);
+        pa[2 * nt + 1] = pack2(p2, p3);
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 1);
+        psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 2);
+        l_run[r] = l_run[r] * alpha[r] + psum[r];
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= alpha[0];
+        o[j][1] *= alpha[0];
+        o[j][2] *= alpha[1];
+        o[j][3] *= alpha[1];
+      }
+      // P (16 heads x 16 keys) as the A fragment: {rows g, keys 2t..}, {g+8, 2t..},
+      // {g, 2t+8..}, {g+8, 2t+8..}
+      const uint32_t pfrag[4] = {pa[0], pa[1], pa[2], pa[3]};
+      // V^T fragments via ldmatrix.trans: matrix mi: keys (mi&1)*8.., dims 8*(2jj + (mi>>1))..
+      const int vrow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + sw_off(vrow, 2 * jj + (mi >> 1)), b0, b1, b2, b3);
+        mma16816(o[2 * jj], pfrag, b0, b1);
+        mma16816(o[2 * jj + 1], pfrag, b2, b3);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // Merge the 4 warps' states through shared memory (reusing the stage buffers).
+  float* sm_o = reinterpret_cast<float*>(smem);                   // [4][16][128]
+  float* sm_m = sm_o + 4 * 16 * 128;                              // [4][16]
+  float* sm_l = sm_m + 4 * 16;                                    // [4][16]
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int col = 8 * j + 2 * t4;
+    sm_o[(warp * 16 + g) * 128 + col] = o[j][0];
+    sm_o[(warp * 16 + g) * 128 + col + 1] = o[j][1];
+    sm_o[(warp * 16 + g + 8) * 128 + col] = o[j][2];
+    sm_o[(warp * 16 + g + 8) * 128 + col + 1] = o[j][3];
+  }
+  if (t4 == 0) {
+    sm_m[warp * 16 + g] = m_run[0];
+    sm_m[warp * 16 + g + 8] = m_run[1];
+    sm_l[warp * 16 + g] = l_run[0];
+    sm_l[warp * 16 + g + 8] = l_run[1];
+  }
+  __syncthreads();
+  // thread -> (head row, 16-dim slab): 16 rows x 8 slabs = 128 threads
+  const int row = tid >> 3, slab = tid & 7;
+  if (row < G) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w * 16 + row]);
+    float wsc[4], L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm_m[w * 16 + row];
+      wsc[w] = (mw == -INFINITY) ? 0.f : ex2f(mw - M);
+      L += wsc[w] * sm_l[w * 16 + row];
+    }
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    float* dst = a.part_o + (static_cast<long long>(item) * a.Hq + hq0 + row) * 128 + slab * 16;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float* src = sm_o + (w * 16 + row) * 128 + slab * 16 + e;
+        acc.x += wsc[w] * src[0];
+        acc.y += wsc[w] * src[1];
+        acc.z += wsc[w] * src[2];
+        acc.w += wsc[w] * src[3];
+      }
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+      *reinterpret_cast<float4*>(dst + e) = acc;
+    }
+    if (slab == 0)
+      a.part_lse[static_cast<long long>(item) * a.Hq + hq0 + row] =
+          L > 0.f ? M + log2f(L) : -INFINITY;
+  }
+}
+
+}  // namespace decode
+
+namespace merge {
+
+struct Args {
+  const float* po;
+  const float* pl;
+  const int* indptr;
+  int P, B, H;
+  int lse_log2;
+  void* out;
+  long long o_sb, o_sh;
+  int out_f32;
+  float* lse_out;
+};
+
+// One warp per (request, head); lane covers 4 dims.
+__global__ void merge_kernel(const Args a) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= a.B * a.H) return;
+  const int b = w / a.H, h = w % a.H;
+  int p0, p1;
+  long long stride_p;  // distance between consecutive parts of this (b, h), in rows of H
+  long long base;
+  if (a.indptr != nullptr) {
+    p0 = a.indptr[b];
+    p1 = a.indptr[b + 1];
+    base = static_cast<long long>(p0) * a.H + h;
+    stride_p = a.H;
+  } else {
+    p0 = 0;
+    p1 = a.P;
+    base = static_cast<long long>(b) * a.H + h;
+    stride_p = static_cast<long long>(a.B) * a.H;
+  }
+  const float cvt = a.lse_log2 ? 1.0f : 1.4426950408889634f;  // to log2
+  float M = -INFINITY;
+  for (int p = p0; p < p1; ++p) M = fmaxf(M, a.pl[base + (p - p0) * stride_p] * cvt);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p = p0; p < p1; ++p) {
+    const long long r = base + (p - p0) * stride_p;
+    const float lp = a.pl[r] * cvt;
+    const float wgt = (lp == -INFINITY) ? 0.f : exp2f(lp - M);
+    L += wgt;
+    const float4 v = *reinterpret_cast<const float4*>(a.po + r * 128 + lane * 4);
+    acc.x += wgt * v.x;
+    acc.y += wgt * v.y;
+    acc.z += wgt * v.z;
+    acc.w += wgt * v.w;
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  const long long o = static_cast<long long>(b) * a.o_sb + static_cast<long long>(h) * a.o_sh + lane * 4;
+  if (a.out_f32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  } else {
+    uint2 pk;
+    pk.x = decode::pack2(acc.x * inv, acc.y * inv);
+    pk.y = decode::pack2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + o) = pk;
+  }
+  if (a.lse_out != nullptr && lane == 0)
+    a.lse_out[static_cast<long long>(b) * a.H + h] =
+        L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
+}
+
+int launch(const Args& a, cudaStream_t stream) {
+  const int warps = a.B * a.H;
+  const int threads = 256;
+  const int blocks = (warps * 32 + threads - 1) / threads;
+  merge_kernel<<<blocks, threads, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
+}
+
+}  // namespace merge
+}  // namespace atf
+
+using namespace atf;
+
+extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host,
+                               int32_t items_capacity, int32_t* item_indptr_host,
+                               AtfDecodePlan* out) {
+  if (p == nullptr || out == nullptr || p->indptr_host == nullptr || p->last_page_len_host == nullptr)
+    return ATF_ERR_INVALID_ARG;
+  if (p->batch_size < 1 || p->num_qo_heads < 1 || p->num_kv_heads < 1 || p->page_size < 1 ||
+      p->num_qo_heads % p->num_kv_heads != 0)
+    return ATF_ERR_INVALID_ARG;
+  if (p->head_dim != ATF_HEAD_DIM) return ATF_ERR_UNSUPPORTED;
+  if (p->num_qo_heads / p->num_kv_heads > 16) return ATF_ERR_UNSUPPORTED;
+  long long total = 0, maxlen = 0;
+  for (int b = 0; b < p->batch_size; ++b) {
+    const int np = p->indptr_host[b + 1] - p->indptr_host[b];
+    const int lpl = p->last_page_len_host[b];
+    if (np < 0) return ATF_ERR_INVALID_ARG;
+    if (np > 0 && (lpl < 1 || lpl > p->page_size)) return ATF_ERR_INVALID_ARG;
+    const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + lpl : 0;
+    if (len > (1ll << 31) - 1) return ATF_ERR_UNSUPPORTED;
+    total += len;
+    maxlen = len > maxlen ? len : maxlen;
+  }
+  int sms = p->num_sms;
+  if (sms <= 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  // Aim for ~8 CTAs per SM in total (2 resident per SM -> ~4 waves), in
+  // 64-key multiples, never below min_chunk keys.
+  const long long target_ctas = 8ll * sms;
+  const long long min_chunk = p->min_chunk_keys > 0 ? p->min_chunk_keys : 256;
+  long long chunk = (total * p->num_kv_heads + target_ctas - 1) / target_ctas;
+  if (chunk < min_chunk) chunk = min_chunk;
+  if (p->max_chunk_keys > 0 && chunk > p->max_chunk_keys) chunk = p->max_chunk_keys;
+  chunk = (chunk + 63) / 64 * 64;
+  if (chunk < 64) chunk = 64;
+  int n = 0;
+  for (int b = 0; b < p->batch_size; ++b) {
+    const int np = p->indptr_host[b + 1] - p->indptr_host[b];
+    const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + p->last_page_len_host[b] : 0;
+    if (item_indptr_host != nullptr) item_indptr_host[b] = n;
+    for (long long k0 = 0; k0 < len; k0 += chunk) {
+      if (items_host != nullptr) {
+        if (n >= items_capacity) return ATF_ERR_WORKSPACE;
+        items_host[4 * n + 0] = b;
+        items_host[4 * n + 1] = static_cast<int32_t>(k0);
+        items_host[4 * n + 2] = static_cast<int32_t>(k0 + chunk < len ? k0 + chunk : len);
+        items_host[4 * n + 3] = 0;
+      }
+      ++n;
+    }
+  }
+  if (item_indptr_host != nullptr) item_indptr_host[p->batch_size] = n;
+  out->num_items = n;
+  out->chunk_keys = static_cast<int32_t>(chunk);
+  out->partial_o_floats = static_cast<int64_t>(n) * p->num_qo_heads * ATF_HEAD_DIM;
+  out->partial_lse_floats = static_cast<int64_t>(n) * p->num_qo_heads;
+  return ATF_OK;
+}
+
+extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
+  if (p == nullptr || p->q == nullptr || p->k_cache == nullptr || p->v_cache == nullptr ||
+      p->indptr == nullptr || p->indices == nullptr || p->last_page_len == nullptr ||
+      p->items == nullptr || p->item_indptr == nullptr || p->partial_o == nullptr ||
+      p->partial_lse == nullptr || p->out == nullptr)
+    return ATF_ERR_INVALID_ARG;
+  if (p->head_dim != ATF_HEAD_DIM) return ATF_ERR_UNSUPPORTED;
+  if (p->batch_size < 1 || p->num_kv_heads < 1 || p->num_qo_heads % p->num_kv_heads != 0 ||
+      p->page_size < 1 || p->num_items < 0)
+    return ATF_ERR_INVALID_ARG;
+  if (p->num_qo_heads / p->num_kv_heads > 16) return ATF_ERR_UNSUPPORTED;
+  if (p->window == ATF_WINDOW_VEC8 && p->qk_layout != ATF_LAYOUT_SORTED_PAIR) return ATF_ERR_UNSUPPORTED;
+  if (p->window < ATF_WINDOW_OFF || p->window > ATF_WINDOW_VEC8) return ATF_ERR_INVALID_ARG;
+  if (p->qk_layout != ATF_LAYOUT_SORTED_PAIR && p->qk_layout != ATF_LAYOUT_ROTATE_HALF)
+    return ATF_ERR_INVALID_ARG;
+  if (!aligned16(p->k_cache) || !aligned16(p->v_cache) || (p->kv_stride_page & 7) ||
+      (p->kv_stride_token & 7) || (p->kv_stride_head & 7))
+    return ATF_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(p->q) & 3) || (p->q_stride_b & 1) || (p->q_stride_h & 1))
+    return ATF_ERR_ALIGNMENT;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc != ATF_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->num_items > 0) {
+    decode::Args a;
+    a.q = static_cast<const __nv_bfloat16*>(p->q);
+    a.q_sb = p->q_stride_b;
+    a.q_sh = p->q_stride_h;
+    a.kc = static_cast<const __nv_bfloat16*>(p->k_cache);
+    a.vc = static_cast<const __nv_bfloat16*>(p->v_cache);
+    a.s_page = p->kv_stride_page;
+    a.s_tok = p->kv_stride_token;
+    a.s_head = p->kv_stride_head;
+    a.indptr = p->indptr;
+    a.indices = p->indices;
+    a.last_page_len = p->last_page_len;
+    a.items = p->items;
+    a.q_pos = p->q_pos;
+    a.kv_pos0 = p->kv_pos0;
+    a.Hq = p->num_qo_heads;
+    a.Hkv = p->num_kv_heads;
+    a.G = p->num_qo_heads / p->num_kv_heads;
+    a.page_size = p->page_size;
+    a.scale_log2 = p->sm_scale * 1.4426950408889634f;
+    a.window = p->window;
+    a.layout = p->qk_layout;
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i) a.zhi16[i] = p->zhi16[i];
+    for (int i = 0; i < ATF_MAX_SLICES; ++i) a.zhi8[i] = p->zhi8[i];
+    a.part_o = p->partial_o;
+    a.part_lse = p->partial_lse;
+    if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             decode::SMEM_BYTES) != cudaSuccess)
+      return ATF_ERR_CUDA;
+    dim3 grid(static_cast<unsigned>(p->num_items), static_cast<unsigned>(p->num_kv_heads));
+    decode::decode_kernel<<<grid, decode::THREADS, decode::SMEM_BYTES, st>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return ATF_ERR_CUDA;
+  }
+  merge::Args m;
+  m.po = p->partial_o;
+  m.pl = p->partial_lse;
+  m.indptr = p->item_indptr;
+  m.P = 0;
+  m.B = p->batch_size;
+  m.H = p->num_qo_heads;
+  m.lse_log2 = 1;
+  m.out = p->out;
+  m.o_sb = p->o_stride_b;
+  m.o_sh = p->o_stride_h;
+  m.out_f32 = p->out_dtype == ATF_DTYPE_F32 ? 1 : 0;
+  m.lse_out = p->lse_out;
+  return merge::launch(m, st);
+}
+
+extern "C" int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream) {
+  if (p == nullptr || p->part_o == nullptr || p->part_lse == nullptr || p->out == nullptr)
+    return ATF_ERR_INVALID_ARG;
+  if (p->head_dim != ATF_HEAD_DIM) return ATF_ERR_UNSUPPORTED;
+  if (p->batch < 1 || p->num_heads < 1 || (p->part_indptr == nullptr && p->num_parts < 1))
+    return ATF_ERR_INVALID_ARG;
+  if (!aligned16(p->part_o) || (p->out_dtype == ATF_DTYPE_F32 && !aligned16(p->out)) ||
+      (reinterpret_cast<uintptr_t>(p->out) & 7) || (p->o_stride_b & 3) || (p->o_stride_h & 3))
+    return ATF_ERR_ALIGNMENT;
+  merge::Args m;
+  m.po = p->part_o;
+  m.pl = p->part_lse;
+  m.indptr = p->part_indptr;
+  m.P = p->num_parts;
+  m.B = p->batch;
+  m.H = p->num_heads;
+  m.lse_log2 = p->lse_log2;
+  m.out = p->out;
+  m.o_sb = p->o_stride_b;
+  m.o_sh = p->o_stride_h;
+  m.out_f32 = p->out_dtype == ATF_DTYPE_F32 ? 1 : 0;
+  m.lse_out = p->lse_out;
+  return merge::launch(m, reinterpret_cast<cudaStream_t>(stream));
+}

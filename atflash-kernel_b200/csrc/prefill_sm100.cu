@@ -1,0 +1,556 @@
+// Windowed causal prefill for sm_100a: warp-specialised tcgen05 / TMEM kernel.
+//
+// One CTA owns two 128-row query tiles (Q0, Q1) of one (batch, q head) and
+// streams the key/value tiles (128 keys) of its causal range:
+//
+//   warp 8       TMA producer. Q once (8 levels x 2 halves per tile); per key
+//                tile only the in-window K levels (L = D_eff/16 of the nearer
+//                query tile) and both 64-dim V boxes.
+//   warp 9       MMA issuer (one lane) and TMEM owner (512 columns):
+//                S_t = Q_t K^T over L(t, j) K-steps of 16 dims into TMEM,
+//                O_t += P_t V with P_t read from TMEM (bf16, aliased on S_t).
+//   warps 0-3/4-7  softmax for Q0 / Q1: one query row per thread, online
+//                softmax in the log2 domain, conditional O rescale, epilogue.
+//
+// The window is the reference's tile quantisation (atflash/reference.py:59-68,
+// atflash/window_table.py:70-76): for query tile q0 and key tile n0 the QK
+// contraction runs over D_eff(z_min) dims with z_min = max(0, q0 - (n0+127));
+// D_eff(z) = 16 * #{i : zhi[i] >= z} (window_tables/atflash_window.py:85-108).
+// The causal diagonal and ragged tails use per-element predicates.
+//
+// Shared memory (1024-aligned):
+//   Q  2 tiles x 8 level slabs x 4 KB. A slab is the canonical no-swizzle
+//      K-major layout: two 2 KB halves (dims 0-7 and 8-15 of the level), each
+//      128 rows x 16 B, so core matrices (8 rows x 16 B) are contiguous:
+//      LBO (K direction) = 2048 B, SBO (8-row groups) = 128 B.
+//   K  2 stages x 8 slabs x 4 KB, same layout.
+//   V  2 stages x 2 boxes (dims 0-63, 64-127) x 128 keys x 128 B, 128B swizzle;
+//      the PV B operand is MN-major: LBO (next 64 dims) = 16 KB, SBO (next 8
+//      keys) = 1 KB.
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+#include <math.h>
+
+#include "atf_internal.h"
+#include "atf_ptx.cuh"
+
+namespace atf {
+namespace prefill {
+
+constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
+constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
+constexpr uint32_t HALF_BYTES = 2048;
+constexpr uint32_t SLAB_BYTES = 2 * HALF_BYTES;
+constexpr uint32_t QTILE_BYTES = 8 * SLAB_BYTES;
+constexpr uint32_t KSTAGE_BYTES = 8 * SLAB_BYTES;
+constexpr uint32_t VBOX_BYTES = BN * 128;
+constexpr uint32_t VSTAGE_BYTES = 2 * VBOX_BYTES;
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + NQ * QTILE_BYTES;
+constexpr uint32_t OFF_V = OFF_K + KST * KSTAGE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + VST * VSTAGE_BYTES;
+
+enum {
+  B_Q = 0,
+  B_KFULL = 1,
+  B_KEMPTY = B_KFULL + KST,
+  B_VFULL = B_KEMPTY + KST,
+  B_VEMPTY = B_VFULL + VST,
+  B_SFULL = B_VEMPTY + VST,
+  B_PFULL = B_SFULL + NQ,
+  B_ODONE = B_PFULL + NQ,
+  B_FINAL = B_ODONE + NQ,
+  NUM_BARS
+};
+constexpr uint32_t OFF_ABORT = OFF_BAR + 8 * NUM_BARS;
+constexpr uint32_t OFF_TMEM = OFF_ABORT + 16;
+constexpr uint32_t SMEM_USED = OFF_TMEM + 16;
+constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // slack for 1024-B alignment
+
+constexpr uint32_t IDESC_QK = make_idesc_bf16(128, 128, 0, 0);
+constexpr uint32_t IDESC_PV = make_idesc_bf16(128, 128, 0, 1);
+constexpr uint32_t FULL = 0xffffffffu;
+
+struct Args {
+  int B, Sq, Sk, Hq, G, n_qblk;
+  long long q_offset;
+  float scale_log2;
+  int causal, layout, window;
+  int zhi[ATF_MAX_LEVELS];
+  __nv_bfloat16* out;
+  long long o_sb, o_ss, o_sh;
+  float* lse;
+  int* err;
+};
+
+__device__ __forceinline__ int levels_for(const Args& a, int row0, int j) {
+  if (!a.window) return 8;
+  long long z = a.q_offset + row0 - (static_cast<long long>(j) * BN + BN - 1);
+  if (z < 0) z = 0;
+  int L = 0;
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi[i]) >= z) ? 1 : 0;
+  return L < 1 ? 1 : L;
+}
+
+__device__ __forceinline__ bool needs_mask(const Args& a, int row0, int j) {
+  const long long n_last = static_cast<long long>(j) * BN + BN - 1;
+  return (a.causal && n_last > a.q_offset + row0) || n_last >= a.Sk;
+}
+
+// Column of the first element of half `hh` of level `i` along head_dim.
+// sorted-pair order: level i = dims [16i, 16i+16).
+// rotate_half order (HF): sorted pairs 8i..8i+7 are HF dims [56-8i, 64-8i) and
+// [120-8i, 128-8i).
+__device__ __forceinline__ int level_col(int layout, int i, int hh) {
+  return layout == ATF_LAYOUT_SORTED_PAIR ? 16 * i + 8 * hh : 64 * hh + 8 * (7 - i);
+}
+
+// Waits with no abort short-cut: used to drain this CTA's own asynchronous
+// copies / MMAs before the CTA's shared memory or TMEM is released.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t sb = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw_u32);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sp + OFF_ABORT);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sp + OFF_TMEM);
+  auto bar = [&](int i) -> uint32_t { return sb + OFF_BAR + 8u * static_cast<uint32_t>(i); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work unit: longest query blocks first; heads of one kv group adjacent.
+  const int nbh = a.B * a.Hq;
+  const int qblk = a.n_qblk - 1 - static_cast<int>(blockIdx.x) / nbh;
+  const int bh = static_cast<int>(blockIdx.x) % nbh;
+  const int bi = bh / a.Hq;
+  const int h = bh % a.Hq;
+  const int hk = h / a.G;
+  int row0[NQ], nk[NQ];
+#pragma unroll
+  for (int t = 0; t < NQ; ++t) {
+    row0[t] = qblk * (BM * NQ) + t * BM;
+    if (row0[t] >= a.Sq) {
+      nk[t] = 0;
+    } else {
+      long long kend = a.causal ? a.q_offset + row0[t] + BM : a.Sk;
+      if (kend > a.Sk) kend = a.Sk;
+      nk[t] = kend > 0 ? static_cast<int>((kend + BN - 1) / BN) : 0;
+    }
+  }
+  const int nk_max = nk[0] > nk[1] ? nk[0] : nk[1];
+
+  if (threadIdx.x == 0) {
+    *s_abort = (a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0) ? 1 : 0;
+    mbar_init(bar(B_Q), 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(bar(B_KFULL + s), 1);
+      mbar_init(bar(B_KEMPTY + s), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(bar(B_VFULL + s), 1);
+      mbar_init(bar(B_VEMPTY + s), 1);
+    }
+    for (int t = 0; t < NQ; ++t) {
+      mbar_init(bar(B_SFULL + t), 1);
+      mbar_init(bar(B_PFULL + t), 128);
+      mbar_init(bar(B_ODONE + t), 1);
+    }
+    mbar_init(bar(B_FINAL), 1);
+    fence_mbar_init();
+  }
+  if (warp == WARP_LOAD && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc(smem_u32(s_tmem), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const AbortCtl ab{s_abort, a.err};
+  const bool start_ok = (*s_abort == 0);
+
+  if (start_ok && warp == WARP_LOAD) {
+    // ---------------------------------------------------------------- producer
+    int issued_k = 0, issued_v = 0;
+    bool ok = true;
+    if (lane == 0) {
+      uint32_t qbytes = 0;
+#pragma unroll
+      for (int t = 0; t < NQ; ++t) qbytes += nk[t] > 0 ? QTILE_BYTES : 0u;
+      mbar_arrive_expect_tx(bar(B_Q), qbytes);
+      for (int t = 0; t < NQ; ++t) {
+        if (nk[t] == 0) continue;
+        for (int i = 0; i < 8; ++i)
+          for (int hh = 0; hh < 2; ++hh)
+            tma_load_4d(sb + OFF_Q + t * QTILE_BYTES + i * SLAB_BYTES + hh * HALF_BYTES, &tmQ,
+                        bar(B_Q), level_col(a.layout, i, hh), row0[t], h, bi);
+      }
+    }
+    for (int j = 0; j < nk_max; ++j) {
+      const int ks = j % KST, vs = j % VST;
+      ok = __all_sync(FULL, mbar_wait(bar(B_KEMPTY + ks), ((j / KST) & 1) ^ 1, ab, kDevErrTimeout));
+      if (!ok) break;
+      if (lane == 0) {
+        int L = 0;
+        for (int t = 0; t < NQ; ++t)
+          if (j < nk[t]) {
+            const int lt = levels_for(a, row0[t], j);
+            L = lt > L ? lt : L;
+          }
+        mbar_arrive_expect_tx(bar(B_KFULL + ks), static_cast<uint32_t>(L) * SLAB_BYTES);
+        for (int i = 0; i < L; ++i)
+          for (int hh = 0; hh < 2; ++hh)
+            tma_load_4d(sb + OFF_K + ks * KSTAGE_BYTES + i * SLAB_BYTES + hh * HALF_BYTES, &tmK,
+                        bar(B_KFULL + ks), level_col(a.layout, i, hh), j * BN, hk, bi);
+      }
+      issued_k = j + 1;
+      __syncwarp();
+      ok = __all_sync(FULL, mbar_wait(bar(B_VEMPTY + vs), ((j / VST) & 1) ^ 1, ab, kDevErrTimeout));
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar(B_VFULL + vs), VSTAGE_BYTES);
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(sb + OFF_V + vs * VSTAGE_BYTES + c * VBOX_BYTES, &tmV, bar(B_VFULL + vs),
+                      64 * c, j * BN, hk, bi);
+      }
+      issued_v = j + 1;
+      __syncwarp();
+    }
+    // Drain: every copy this warp issued must land before shared memory is
+    // released (no-op on the normal path, where the MMA warp consumed them).
+    drain_wait(bar(B_Q), 0);
+    for (int j = issued_k - KST; j < issued_k; ++j)
+      if (j >= 0) drain_wait(bar(B_KFULL + j % KST), (j / KST) & 1);
+    for (int j = issued_v - VST; j < issued_v; ++j)
+      if (j >= 0) drain_wait(bar(B_VFULL + j % VST), (j / VST) & 1);
+    __syncwarp();
+  } else if (start_ok && warp == WARP_MMA) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint32_t qbase = sb + OFF_Q, kbase = sb + OFF_K, vbase = sb + OFF_V;
+    auto issue_S = [&](int t, int j) {
+      const int ks = j % KST;
+      const int L = levels_for(a, row0[t], j);
+      const uint32_t d_tmem = tmem + static_cast<uint32_t>(t * 128);
+      for (int i = 0; i < L; ++i) {
+        const uint64_t ad = make_sdesc(qbase + t * QTILE_BYTES + i * SLAB_BYTES, HALF_BYTES, 128,
+                                       kLayoutNone);
+        const uint64_t bd = make_sdesc(kbase + ks * KSTAGE_BYTES + i * SLAB_BYTES, HALF_BYTES, 128,
+                                       kLayoutNone);
+        mma_ss(d_tmem, ad, bd, IDESC_QK, i > 0 ? 1u : 0u);
+      }
+      tc_commit(bar(B_SFULL + t));
+    };
+    auto issue_PV = [&](int t, int j) {
+      const int vs = j % VST;
+      const uint32_t o_tmem = tmem + 256u + static_cast<uint32_t>(t * 128);
+      const uint32_t p_tmem = tmem + static_cast<uint32_t>(t * 128);
+      for (int c = 0; c < BN / 16; ++c) {
+        const uint64_t bd =
+            make_sdesc(vbase + vs * VSTAGE_BYTES + c * 2048, VBOX_BYTES, 1024, kLayoutSw128);
+        mma_ts(o_tmem, p_tmem + static_cast<uint32_t>(c * 8), bd, IDESC_PV,
+               (j > 0 || c > 0) ? 1u : 0u);
+      }
+      tc_commit(bar(B_ODONE + t));
+    };
+    bool ok = __all_sync(FULL, mbar_wait(bar(B_Q), 0, ab, kDevErrTimeout));
+    tc_fence_after();
+    if (ok && nk_max > 0) {
+      ok = __all_sync(FULL, mbar_wait(bar(B_KFULL + 0), 0, ab, kDevErrTimeout));
+      tc_fence_after();
+      if (ok && lane == 0) {
+        for (int t = 0; t < NQ; ++t)
+          if (nk[t] > 0) issue_S(t, 0);
+        tc_commit(bar(B_KEMPTY + 0));
+      }
+      __syncwarp();
+    }
+    for (int j = 0; ok && j < nk_max; ++j) {
+      const int vs = j % VST;
+      ok = __all_sync(FULL, mbar_wait(bar(B_VFULL + vs), (j / VST) & 1, ab, kDevErrTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      bool kwaited = false;
+#pragma unroll
+      for (int t = 0; t < NQ; ++t) {
+        if (!ok) break;
+        if (j < nk[t]) {
+          ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + t), j & 1, ab, kDevErrTimeout));
+          if (!ok) break;
+          tc_fence_after();
+          if (lane == 0) issue_PV(t, j);
+          __syncwarp();
+        }
+        if (j + 1 < nk[t]) {
+          if (!kwaited) {
+            const int ks = (j + 1) % KST;
+            ok = __all_sync(FULL,
+                            mbar_wait(bar(B_KFULL + ks), ((j + 1) / KST) & 1, ab, kDevErrTimeout));
+            if (!ok) break;
+            tc_fence_after();
+            kwaited = true;
+          }
+          if (lane == 0) issue_S(t, j + 1);
+          __syncwarp();
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) {
+        if (kwaited) tc_commit(bar(B_KEMPTY + (j + 1) % KST));
+        tc_commit(bar(B_VEMPTY + vs));
+      }
+      __syncwarp();
+    }
+    // Every MMA issued by this CTA completes before TMEM is released.
+    if (lane == 0) tc_commit(bar(B_FINAL));
+    __syncwarp();
+    drain_wait(bar(B_FINAL), 0);
+    __syncwarp();
+  } else if (start_ok && warp < 8) {
+    // ---------------------------------------------------------------- softmax
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + static_cast<uint32_t>(t * 128) + lane_off;
+    const uint32_t tO = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_off;
+    const int my_row0 = t ? row0[1] : row0[0];
+    const int my_nk = t ? nk[1] : nk[0];
+    const int qrow = my_row0 + r;
+    const long long qpos = a.q_offset + qrow;
+    const float sl2 = a.scale_log2;
+    float m2 = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < my_nk; ++j) {
+      ok = __all_sync(FULL, mbar_wait(bar(B_SFULL + t), j & 1, ab, kDevErrTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t rr[32];
+        tmem_ld32(tS + static_cast<uint32_t>(32 * c4), rr);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[32 * c4 + e] = __uint_as_float(rr[e]);
+      }
+      if (needs_mask(a, my_row0, j)) {
+        const long long n0 = static_cast<long long>(j) * BN;
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const long long key = n0 + c;
+          if ((a.causal && key > qpos) || key >= a.Sk) s[c] = -INFINITY;
+        }
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int c = 4; c < BN; c += 4) {
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
+        mx2 = fmaxf(mx2, s[c + 2]);
+        mx3 = fmaxf(mx3, s[c + 3]);
+      }
+      const float mnew = fmaxf(m2, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+      // Lazy rescale: the running max only moves when it grows by more than
+      // 8 (log2 units), so P <= 2^8 stays exact enough in bf16 and O is
+      // rescaled rarely. The O update itself happens after P is stored.
+      float alpha = 1.0f;
+      bool need = false;
+      if (j == 0) {
+        m2 = mnew;
+      } else {
+        need = mnew > m2 + 8.0f;
+        if (need) {
+          alpha = ex2_approx(m2 - mnew);
+          l *= alpha;
+          m2 = mnew;
+        }
+      }
+      const float msub = (m2 == -INFINITY) ? 0.f : m2;
+      float ls0 = 0.f, ls1 = 0.f;
+      uint32_t pk0[32], pk1[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -msub));
+        const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
+        ls0 += p0;
+        ls1 += p1;
+        pk0[c] = pack_bf16x2(p0, p1);
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2_approx(fmaf(s[64 + 2 * c], sl2, -msub));
+        const float p1 = ex2_approx(fmaf(s[64 + 2 * c + 1], sl2, -msub));
+        ls0 += p0;
+        ls1 += p1;
+        pk1[c] = pack_bf16x2(p0, p1);
+      }
+      l += ls0 + ls1;
+      tmem_st32(tS, pk0);
+      tmem_st32(tS + 32u, pk1);
+      if (__any_sync(FULL, need)) {
+        // O holds the sum up to tile j-1 once PV(t, j-1) has completed; PV(t, j)
+        // is not issued before this warpgroup arrives on PFULL below.
+        ok = __all_sync(FULL, mbar_wait(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c4 = 0; c4 < HD / 32; ++c4) {
+          uint32_t rr[32];
+          tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+          tmem_st32(tO + static_cast<uint32_t>(32 * c4), rr);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar(B_PFULL + t));
+    }
+    if (ok && my_nk > 0) {
+      ok = __all_sync(FULL, mbar_wait(bar(B_ODONE + t), (my_nk - 1) & 1, ab, kDevErrTimeout));
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        const bool store = qrow < a.Sq;
+        __nv_bfloat16* orow = a.out + static_cast<long long>(bi) * a.o_sb +
+                              static_cast<long long>(qrow) * a.o_ss +
+                              static_cast<long long>(h) * a.o_sh;
+#pragma unroll
+        for (int c4 = 0; c4 < HD / 32; ++c4) {
+          uint32_t rr[32];
+          tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pk[e] = pack_bf16x2(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
+          if (store) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c4);
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+          }
+        }
+        if (a.lse != nullptr && store)
+          a.lse[(static_cast<long long>(bi) * a.Hq + h) * a.Sq + qrow] =
+              (m2 + log2f(l)) * 0.69314718055994531f;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace prefill
+}  // namespace atf
+
+using namespace atf;
+
+extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
+  using namespace atf::prefill;
+  if (p == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr || p->out == nullptr)
+    return ATF_ERR_INVALID_ARG;
+  if (p->head_dim != ATF_HEAD_DIM) return ATF_ERR_UNSUPPORTED;
+  if (p->batch < 1 || p->seqlen_q < 1 || p->seqlen_k < 1 || p->num_heads_q < 1 ||
+      p->num_heads_kv < 1 || p->num_heads_q % p->num_heads_kv != 0)
+    return ATF_ERR_INVALID_ARG;
+  if (p->seqlen_q > (1ll << 30) || p->seqlen_k > (1ll << 30) || p->batch * p->num_heads_q > (1 << 20))
+    return ATF_ERR_UNSUPPORTED;
+  if (p->causal && p->q_offset < 0) return ATF_ERR_UNSUPPORTED;
+  if (p->q_offset < 0 || p->q_offset + p->seqlen_q > (1ll << 31)) return ATF_ERR_INVALID_ARG;
+  if (p->qk_layout != ATF_LAYOUT_SORTED_PAIR && p->qk_layout != ATF_LAYOUT_ROTATE_HALF)
+    return ATF_ERR_INVALID_ARG;
+  if (p->window != ATF_WINDOW_OFF && p->window != ATF_WINDOW_SNAP16) return ATF_ERR_UNSUPPORTED;
+  if (!(p->softmax_scale > 0.f)) return ATF_ERR_INVALID_ARG;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out))
+    return ATF_ERR_ALIGNMENT;
+  const int64_t strides[12] = {p->q_stride_b, p->q_stride_s, p->q_stride_h, p->k_stride_b,
+                               p->k_stride_s, p->k_stride_h, p->v_stride_b, p->v_stride_s,
+                               p->v_stride_h, p->o_stride_b, p->o_stride_s, p->o_stride_h};
+  for (int i = 0; i < 12; ++i)
+    if (strides[i] < 0 || (strides[i] & 7) != 0) return ATF_ERR_ALIGNMENT;
+  if (p->window == ATF_WINDOW_SNAP16) {
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i)
+      if (p->zhi[i] < 0) return ATF_ERR_INVALID_ARG;
+    // zhi[0] must cover the largest distance in the problem (D_eff >= 16 always).
+    if (static_cast<int64_t>(p->zhi[0]) < p->q_offset + p->seqlen_q - 1) return ATF_ERR_INVALID_ARG;
+  }
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc != ATF_OK) return rc;
+
+  CUtensorMap tq, tk, tv;
+  auto sane = [](int64_t stride, int64_t size) -> uint64_t {
+    // Size-1 dims may carry any stride; use a valid placeholder.
+    return static_cast<uint64_t>(size == 1 ? 16 : stride * 2);
+  };
+  {
+    const uint64_t dims[4] = {128, (uint64_t)p->seqlen_q, (uint64_t)p->num_heads_q, (uint64_t)p->batch};
+    const uint64_t str[3] = {sane(p->q_stride_s, p->seqlen_q), sane(p->q_stride_h, p->num_heads_q),
+                             sane(p->q_stride_b, p->batch)};
+    const uint32_t box[4] = {8, BM, 1, 1};
+    if ((rc = encode_tiled_bf16(&tq, p->q, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != ATF_OK)
+      return rc;
+  }
+  {
+    const uint64_t dims[4] = {128, (uint64_t)p->seqlen_k, (uint64_t)p->num_heads_kv, (uint64_t)p->batch};
+    const uint64_t str[3] = {sane(p->k_stride_s, p->seqlen_k), sane(p->k_stride_h, p->num_heads_kv),
+                             sane(p->k_stride_b, p->batch)};
+    const uint32_t box[4] = {8, BN, 1, 1};
+    if ((rc = encode_tiled_bf16(&tk, p->k, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != ATF_OK)
+      return rc;
+  }
+  {
+    const uint64_t dims[4] = {128, (uint64_t)p->seqlen_k, (uint64_t)p->num_heads_kv, (uint64_t)p->batch};
+    const uint64_t str[3] = {sane(p->v_stride_s, p->seqlen_k), sane(p->v_stride_h, p->num_heads_kv),
+                             sane(p->v_stride_b, p->batch)};
+    const uint32_t box[4] = {64, BN, 1, 1};
+    if ((rc = encode_tiled_bf16(&tv, p->v, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
+      return rc;
+  }
+
+  Args a;
+  a.B = static_cast<int>(p->batch);
+  a.Sq = static_cast<int>(p->seqlen_q);
+  a.Sk = static_cast<int>(p->seqlen_k);
+  a.Hq = static_cast<int>(p->num_heads_q);
+  a.G = static_cast<int>(p->num_heads_q / p->num_heads_kv);
+  a.n_qblk = static_cast<int>((p->seqlen_q + BM * NQ - 1) / (BM * NQ));
+  a.q_offset = p->q_offset;
+  a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.causal = p->causal ? 1 : 0;
+  a.layout = p->qk_layout;
+  a.window = p->window == ATF_WINDOW_SNAP16 ? 1 : 0;
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) a.zhi[i] = p->zhi[i];
+  a.out = static_cast<__nv_bfloat16*>(p->out);
+  a.o_sb = p->o_stride_b;
+  a.o_ss = p->o_stride_s;
+  a.o_sh = p->o_stride_h;
+  a.lse = p->lse;
+  a.err = p->error_flag;
+
+  if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(SMEM_BYTES)) != cudaSuccess)
+    return ATF_ERR_CUDA;
+  const long long grid = static_cast<long long>(a.n_qblk) * a.B * a.Hq;
+  if (grid > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
+  prefill_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES,
+                   reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, a);
+  return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
+}

@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Benchmark of the windowed-attention hot path (one JSON line on rank 0).
+
+Workload: windowed causal prefill, Qwen2.5-7B-1M attention
+shape 28 q / 4 kv heads, head_dim 128, theta 1e7, window k=2, batch 1,
+N = 131072, bf16; q/k/v ~ N(0,1) seeded on the device and taken as post-RoPE
+sorted-pair tensors (the reference's microbench convention,
+microbench/b1_bench_protocol.py:144-158). A step = one full prefill.
+
+  --gpus N  (torchrun, one rank per GPU): the query rows are split into 2N
+            zig-zag blocks; each rank computes its two blocks against replicated
+            K/V (no collective on the data path). Total work is fixed
+            (strong scaling); value = max-over-ranks ms per full prefill.
+  --impl reference  times the CPU restatement of the reference's oracle
+            (oracle/, numpy, all host threads) on a bounded sample of the same
+            workload, extrapolated by FLOP count; rank 0 only.
+
+Extra fields: window-off and k=64 prefill times, the on/off ratio against the
+2/(1+s) ceiling, and the windowed paged decode of BASELINE config 3 (batch 8,
+24/8 heads, 128K context, page 16) with its HBM roofline.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "atflash-kernel_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+N_CTX, HQ, HKV, D, THETA, K_RET = 131072, 28, 4, 128, 1e7, 2.0
+METRIC = "Windowed-attn prefill ms @128K/512K + decode µs/step @128K, window on vs off"
+# dram bytes of one prefill launch from ncu (profiles/prefill_sm100_128k.md); None = not captured
+PREFILL_TRAFFIC_BYTES = None
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps, warmup, world, stream=None, sampler=None):
+    """W warm-up calls, then K calls between two barriers + syncs, timed with
+    CUDA events on the launching stream; returns ms per step (max over ranks)."""
+    stream = stream or torch.cuda.current_stream()
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    ms = e0.elapsed_time(e1) / steps
+    return max_over_ranks(ms, world), clocks
+
+
+def prefill_inputs(device, copies=2, seed=2026):
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(copies):
+        q = torch.randn((1, N_CTX, HQ, D), generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn((1, N_CTX, HKV, D), generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn((1, N_CTX, HKV, D), generator=g, device=device).to(torch.bfloat16)
+        out.append((q, k, v))
+    return out
+
+
+def cpu_baseline_sample(n_tiles=4, heads=7, k_ret=K_RET):
+    """Time the numpy oracle on `n_tiles` query tiles x `heads` heads (one kv
+    group) of the config-2 workload; extrapolate to the full prefill by FLOPs."""
+    import numpy as np
+    from oracle import attention as OA
+    from oracle import window_table as OWT
+    from atflash import window_table as WT
+    rng = np.random.default_rng(0)
+    w = OWT.wavelengths_sorted(D, THETA, k_ret)
+    zhi = WT.window_zhi_from_kret(D, THETA, k_ret, 2 ** 31 - 1)
+    total = WT.prefill_work(HQ, N_CTX, N_CTX, zhi)["flops"]
+    tiles = [int((i + 0.5) * (N_CTX // 128) / n_tiles) for i in range(n_tiles)]
+    sec = 0.0
+    flops = 0.0
+    for t in tiles:
+        hi = (t + 1) * 128
+        q = rng.standard_normal((1, heads, 128, D), dtype=np.float32)
+        k = rng.standard_normal((1, 1, hi, D), dtype=np.float32)
+        v = rng.standard_normal((1, 1, hi, D), dtype=np.float32)
+        t0 = time.perf_counter()
+        OA.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128, q_offset=t * 128)
+        sec += time.perf_counter() - t0
+        flops += WT.prefill_work(heads, 128, hi, zhi, q_offset=t * 128)["flops"]
+    ms_full = sec * (total / flops) * 1e3
+    return ms_full, {"cores": os.cpu_count(), "kind": "port",
+                     "sample": f"numpy oracle (oracle/attention.py) on query tiles {tiles} x {heads} heads "
+                               f"of the 131072-token config-2 prefill, extrapolated by windowed FLOPs "
+                               f"({flops:.3g} of {total:.3g}); {sec:.2f} s of CPU work"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    samples = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        ms, info = cpu_baseline_sample(n_tiles=2, heads=7)
+        if i >= args.warmup:
+            samples.append(ms)
+    v = statistics.median(samples)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+            "config": {"workload": "prefill N=131072 Hq=28 Hkv=4 d=128 theta=1e7 k=2 (BASELINE config 2)",
+                       "batch": 1, "seq_len": N_CTX},
+            "cpu_baseline": dict(info, value=v, unit="ms"),
+            "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def bench_decode(device, steps, warmup, peaks):
+    """BASELINE config 3 at 128K: batch 8, 24/8 heads, page 16, theta 5e5, k=2 vs off."""
+    import atflash
+    from atflash import window_table as WT
+    B, hq, hkv, page, N = 8, 24, 8, 16, 131072
+    npg = N // page
+    total = B * npg
+    g = torch.Generator(device="cpu").manual_seed(1234 + N + D)
+    perm = torch.randperm(total, generator=g).to(torch.int32)
+    gd = torch.Generator(device=device).manual_seed(99)
+    kc = torch.randn((total, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    vc = torch.randn((total, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    q = torch.randn((B, hq, D), generator=gd, device=device).to(torch.bfloat16)
+    indptr = torch.arange(0, total + 1, npg, dtype=torch.int32)
+    lpl = torch.full((B,), page, dtype=torch.int32)
+    ws = torch.empty(128 * 1024 * 1024, dtype=torch.uint8, device=device)
+    res = {}
+    for name, wt in (("on", atflash.WindowTable(D, 5e5, 2.0)), ("off", None)):
+        w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt)
+        out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=device)
+        ms, _ = timed(lambda i: w.run(q, (kc, vc), out=out), steps, warmup, 1)
+        zhi = wt.zhi16 if wt is not None else None
+        byts = WT.decode_bytes(hkv, [N] * B, zhi)["bytes"]
+        res[name] = {"us": ms * 1e3, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9}
+    res["ratio_on_off"] = res["off"]["us"] / res["on"]["us"]
+    res["hbm_frac_on"] = res["on"]["gbs"] / peaks["hbm_gbs"]
+    del kc, vc
+    torch.cuda.empty_cache()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="atflash", choices=["atflash", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip off/k64/decode/e2e/cpu legs")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        # CPU arm: rank 0 alone times the oracle port; other ranks exit without work
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, world, local = setup_dist(args.gpus)
+    import atflash
+    from atflash import window_table as WT
+    device = torch.device("cuda", local)
+    peaks = load_peaks()
+    inputs = prefill_inputs(device)
+    wt2 = atflash.WindowTable(D, THETA, K_RET)
+    blocks = atflash.dist.zigzag_blocks(N_CTX, world, rank) if world > 1 else [(0, N_CTX)]
+    out = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16, device=device)
+    launches_per_step = len([b for b in blocks if b[1] > b[0]])
+
+    def step(wt):
+        def fn(i):
+            q, k, v = inputs[i % len(inputs)]
+            for (s, e) in blocks:
+                if e > s:
+                    atflash.prefill_fwd(q[:, s:e], k[:, :e], v[:, :e], causal=True, window_table=wt,
+                                        q_offset=s, out=out[:, s:e])
+        return fn
+
+    sampler = ClockSampler(local)
+    ms_on, clocks = timed(step(wt2), args.steps, args.warmup, world, sampler=sampler)
+    err = atflash.check_device_errors()
+    work_on = WT.prefill_work(HQ, N_CTX, N_CTX, wt2.zhi16)
+    # per-rank work for the roofline of this rank's launches
+    my_flops = sum(WT.prefill_work(HQ, e - s, e, wt2.zhi16, q_offset=s)["flops"] for (s, e) in blocks if e > s)
+    extras = {}
+    if not args.no_extras:
+        ms_off, _ = timed(step(None), args.steps, args.warmup, world)
+        wt64 = atflash.WindowTable(D, THETA, 64.0)
+        ms_64, _ = timed(step(wt64), args.steps, args.warmup, world)
+        work_64 = WT.prefill_work(HQ, N_CTX, N_CTX, wt64.zhi16)
+        extras["prefill"] = {
+            "k2_ms": ms_on, "off_ms": ms_off, "k64_ms": ms_64,
+            "ratio_on_off_k2": ms_off / ms_on, "ceiling_k2": work_on["ceiling"], "s_k2": work_on["s"],
+            "ceiling_recovery_k2": (ms_off / ms_on - 1) / (work_on["ceiling"] - 1),
+            "ratio_on_off_k64": ms_off / ms_64, "ceiling_k64": work_64["ceiling"],
+            "tflops_k2_algorithmic": work_on["flops"] / (ms_on * 1e-3) / 1e12,
+            "tflops_off": work_on["flops_dense"] / (ms_off * 1e-3) / 1e12,
+            "tflops_k64_algorithmic": work_64["flops"] / (ms_64 * 1e-3) / 1e12,
+        }
+    # e2e through the public API with host buffers: H2D of q/k/v, prefill, D2H of out
+    e2e = None
+    if not args.no_extras:
+        qh = [t.cpu().pin_memory() for t in inputs[0]]
+        outh = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16).pin_memory()
+        qd, kd, vd = (torch.empty_like(t, device=device) for t in qh)
+        h2d = sum(t.numel() * t.element_size() for t in qh)
+        d2h = 0
+        for (s, e) in blocks:
+            d2h += (e - s) * HQ * D * 2
+
+        def e2e_fn(i):
+            qd.copy_(qh[0], non_blocking=True)
+            kd.copy_(qh[1], non_blocking=True)
+            vd.copy_(qh[2], non_blocking=True)
+            for (s, e) in blocks:
+                if e > s:
+                    o = atflash.flash_attn_func(qd[:, s:e], kd[:, :e], vd[:, :e], causal=True,
+                                                window_table=wt2, q_offset=s)
+                    outh[:, s:e].copy_(o, non_blocking=True)
+        ms_e2e, _ = timed(e2e_fn, max(2, args.steps // 2), 3, world)
+        e2e = {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        del qd, kd, vd
+    decode = None
+    if not args.no_extras and rank == 0 and world == 1:
+        del inputs
+        torch.cuda.empty_cache()
+        decode = bench_decode(device, 20, 5, peaks)
+    cpu = None
+    if not args.no_extras and rank == 0 and world == 1:
+        cms, info = cpu_baseline_sample()
+        cpu = dict(info, value=cms, unit="ms")
+    if rank == 0:
+        achieved = my_flops / (ms_on * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"],
+                "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
+                "peak_source": peaks["source"] + " (burst; kernel timed alone)",
+                "traffic": PREFILL_TRAFFIC_BYTES,
+                "work": "windowed FLOPs 2*Hq*sum_unmasked(D_eff(tile)+d) per launch set of this rank",
+                "flops_per_step": my_flops}
+        line = {"metric": METRIC, "value": ms_on, "unit": "ms", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_on, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1) bf16, seeded on device",
+                "config": {"workload": "prefill N=131072 Hq=28 Hkv=4 d=128 theta=1e7 k=2 (BASELINE config 2)",
+                           "batch": 1, "seq_len": N_CTX, "window_k": K_RET, "tiles": "128x128",
+                           "parallelism": f"zigzag query shards x{world}, K/V replicated",
+                           "l2": "inputs 1.2 GB per copy > 126 MB L2; two copies rotated"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
+                "device_error_flag": err, "extras": dict(extras, decode=decode) if extras else None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

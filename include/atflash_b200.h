@@ -1,0 +1,227 @@
+/*
+ * atflash_b200.h -- C ABI of the B200 (sm_100a) windowed-attention library.
+ *
+ * Windowed attention (ATFlash): RoPE pair r keeps its QK^T term only while the
+ * query-key distance z <= w_r = k * lambda_r; softmax and P.V are unchanged.
+ * With the pairs stored in wavelength-sorted order the kept pairs form a prefix
+ * of the head dimension, so the window shortens the QK contraction to
+ * D_eff(z) = 16 * #{i : zhi[i] >= z} dims (a 16-dim "level" per MMA K-step).
+ *
+ * Conventions
+ *  - Every function returns 0 (ATF_OK) or a negative ATF_ERR_* code; nothing
+ *    aborts, nothing synchronises the device unless its comment says so.
+ *  - All tensor pointers are device pointers owned by the caller; strides are
+ *    in elements and the innermost (head_dim) stride is 1.
+ *  - Kernels run on the caller's stream. The library keeps no mutable global
+ *    state except the lazily loaded driver entry point used to encode TMA
+ *    descriptors.
+ *  - head_dim is 128. GQA group sizes 1..16 (1/2/3/4/7/8 are the tested ones).
+ *  - Device-side waits are bounded. A wait that expires writes a non-zero code
+ *    to params->error_flag (if not NULL) and the kernel returns early; read it
+ *    with atf_read_error_flag() after synchronising.
+ *
+ * Reference interfaces each entry point replaces (paths inside the reference
+ * project):
+ *  atf_window_*      atflash/window_table.py:38-128, window_tables/atflash_window.py:52-116,
+ *                    kernels/flashinfer_port/fiwin_common.py:35-60
+ *  atf_prefill_fwd   the windowed FA4 forward, called as
+ *                    _flash_attn_fwd(q, k, v, causal=True, pack_gqa=..., atflash_window_zhi=zhi)
+ *                    at e2e_pipeline/atflash_e2e_fafi.py:119 and microbench/b1_correctness.py:84-85
+ *  atf_decode_plan / atf_decode_run
+ *                    the windowed FlashInfer decode, called as
+ *                    single_decode_with_kv_cache_with_jit_module(mod, q, k, v, None, zhi8, ...)
+ *                    at e2e_pipeline/atflash_e2e_fafi.py:106-110 (kernel diff:
+ *                    kernels/flashinfer_port/decode.cuh.diff:51-89); batched and paged here
+ *  atf_lse_merge     the split-KV state merge inside that FlashInfer decode
+ *                    (kernels/flashinfer_port/decode.cuh.diff:62 kv_chunk_size)
+ *  atf_rope_pack     the HF RoPE + sorted-pair permutation the harness applies before the
+ *                    kernels (e2e_pipeline/atflash_e2e_fafi.py:186-194,
+ *                    microbench/b1_correctness.py:113-135)
+ */
+#ifndef ATFLASH_B200_H_
+#define ATFLASH_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* atf_stream_t; /* identical to cudaStream_t */
+
+enum {
+  ATF_OK = 0,
+  ATF_ERR_INVALID_ARG = -1,  /* null pointer, bad shape, bad stride */
+  ATF_ERR_UNSUPPORTED = -2,  /* valid but unsupported (head_dim, group size, ...) */
+  ATF_ERR_ALIGNMENT = -3,    /* pointer or stride not 16-byte aligned */
+  ATF_ERR_CUDA = -4,         /* a CUDA runtime / driver call failed */
+  ATF_ERR_WORKSPACE = -5,    /* workspace or plan buffer too small */
+  ATF_ERR_DEVICE = -6,       /* device is not sm_100 */
+  ATF_ERR_TIMEOUT = -7       /* value written to error_flag by an expired device wait */
+};
+
+enum { ATF_LAYOUT_SORTED_PAIR = 0, ATF_LAYOUT_ROTATE_HALF = 1 };
+enum { ATF_KV_NHD = 0, ATF_KV_HND = 1 };
+enum { ATF_WINDOW_OFF = 0, ATF_WINDOW_SNAP16 = 1, ATF_WINDOW_VEC8 = 2 };
+enum { ATF_DTYPE_BF16 = 0, ATF_DTYPE_F32 = 1 };
+
+#define ATF_HEAD_DIM 128
+#define ATF_MAX_LEVELS 8  /* head_dim / 16 */
+#define ATF_MAX_SLICES 16 /* head_dim / 8  */
+
+/* ------------------------------------------------------------------ tables */
+
+/* fp32 window width of every sorted pair j: k * 2pi * base^(2(P-1-j)/d),
+ * computed in fp64 and rounded to fp32; k_ret = +inf gives +inf. Writes d/2
+ * floats. Replaces atflash/window_table.py:38-54. */
+int atf_window_widths(int head_dim, double rope_base, double k_ret, float* wvec_out);
+
+/* zhi[i] = max{z >= 0 : D_eff(z) >= 16(i+1)}, capped at n_ctx (d/16 entries).
+ * wvec holds d/2 widths in any order. Replaces window_tables/atflash_window.py:85-116. */
+int atf_window_zhi16(const float* wvec, int head_dim, int64_t n_ctx, int32_t* zhi_out);
+
+/* vec8 slice table: zhi8[tx] = floor(w[4 tx]) (INT32_MAX for inf), d/8 entries.
+ * Replaces kernels/flashinfer_port/fiwin_common.py:35-46. */
+int atf_window_zhi8(const float* wvec, int head_dim, int32_t* zhi_out);
+
+/* D_eff (dims) at distance z from a 16-snap zhi table. Replaces
+ * atflash/window_table.py:62-67 evaluated through the zhi levels. */
+int atf_window_deff(const int32_t* zhi16, int n_levels, int64_t z);
+
+/* ------------------------------------------------------------------ prefill */
+
+typedef struct {
+  const void* q; /* bf16 [B, Sq, Hq, 128] (BSHD; strides below) */
+  const void* k; /* bf16 [B, Sk, Hkv, 128] */
+  const void* v; /* bf16 [B, Sk, Hkv, 128] */
+  void* out;     /* bf16 [B, Sq, Hq, 128] */
+  float* lse;    /* optional fp32 [B, Hq, Sq], natural log of sum(exp(scale*s)) */
+  int64_t batch, seqlen_q, seqlen_k, num_heads_q, num_heads_kv, head_dim;
+  int64_t q_stride_b, q_stride_s, q_stride_h;
+  int64_t k_stride_b, k_stride_s, k_stride_h;
+  int64_t v_stride_b, v_stride_s, v_stride_h;
+  int64_t o_stride_b, o_stride_s, o_stride_h;
+  int64_t q_offset;    /* global position of query row 0; keys are at 0..Sk-1.
+                          Causal masking keeps key n for row i iff n <= q_offset + i. */
+  float softmax_scale; /* usually 1/sqrt(head_dim) */
+  int causal;
+  int qk_layout;       /* ATF_LAYOUT_*: pair order of q and k along head_dim */
+  int window;          /* ATF_WINDOW_OFF or ATF_WINDOW_SNAP16 */
+  int32_t zhi[ATF_MAX_LEVELS]; /* 16-snap levels; zhi[0] must cover every distance */
+  int* error_flag;     /* optional device int (see header comment) */
+} AtfPrefillParams;
+
+/* Windowed causal prefill on the tcgen05/TMEM kernel. Tiles are 128 queries x
+ * 128 keys; the window is quantised per (q-tile, k-tile) at the tile's smallest
+ * distance, as atflash/reference.py:27-80 with block_m = block_n = 128. */
+int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream);
+
+/* ------------------------------------------------------------------ decode */
+
+typedef struct {
+  int32_t batch_size;
+  int32_t num_qo_heads, num_kv_heads, head_dim, page_size;
+  const int32_t* indptr_host;        /* [batch+1] page ranges per request (host) */
+  const int32_t* last_page_len_host; /* [batch] (host) */
+  int32_t num_sms;        /* 0: query the current device */
+  int32_t min_chunk_keys; /* 0: default (256) */
+  int32_t max_chunk_keys; /* 0: unlimited; forces at least ceil(len/max) splits */
+} AtfDecodePlanParams;
+
+typedef struct {
+  int32_t num_items;       /* work items (request, key range) */
+  int32_t chunk_keys;      /* keys per item (multiple of 64) */
+  int64_t partial_o_floats;   /* workspace floats needed for partial outputs */
+  int64_t partial_lse_floats; /* workspace floats needed for partial LSEs */
+} AtfDecodePlan;
+
+/* Build the split-KV schedule on the host. items_host receives num_items rows
+ * of int32[4] = {request, key_begin, key_end, 0}; item_indptr_host receives
+ * batch+1 offsets. Pass NULL buffers to query sizes only. */
+int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host, int32_t items_capacity,
+                    int32_t* item_indptr_host, AtfDecodePlan* out);
+
+typedef struct {
+  const void* q; /* bf16 [B, Hq, 128] */
+  int64_t q_stride_b, q_stride_h;
+  const void* k_cache; /* bf16 pages: NHD [P, page, Hkv, 128] or HND [P, Hkv, page, 128] */
+  const void* v_cache;
+  int64_t kv_stride_page, kv_stride_token, kv_stride_head; /* same for k and v */
+  int kv_layout;        /* ATF_KV_* (informational; strides carry the layout) */
+  int qk_layout;        /* pair order of q and the cached k */
+  const int32_t* indptr;        /* device [B+1] */
+  const int32_t* indices;       /* device [nnz_pages] */
+  const int32_t* last_page_len; /* device [B] */
+  const int32_t* items;         /* device, from atf_decode_plan */
+  const int32_t* item_indptr;   /* device [B+1] */
+  int32_t num_items;
+  int32_t batch_size, num_qo_heads, num_kv_heads, head_dim, page_size;
+  const int64_t* q_pos;   /* optional device [B]: global position of the query (default kv_len-1) */
+  const int64_t* kv_pos0; /* optional device [B]: global position of local key 0 (default 0) */
+  float sm_scale;
+  int window;                          /* ATF_WINDOW_OFF / SNAP16 / VEC8 */
+  int32_t zhi16[ATF_MAX_LEVELS];       /* SNAP16: per-key 16-dim levels */
+  int32_t zhi8[ATF_MAX_SLICES];        /* VEC8: per 8-dim slice (sorted-pair layout only) */
+  float* partial_o;   /* workspace [num_items, Hq, 128] fp32 */
+  float* partial_lse; /* workspace [num_items, Hq] fp32 (log2 domain) */
+  void* out;          /* [B, Hq, 128], bf16 or fp32 per out_dtype */
+  int64_t o_stride_b, o_stride_h;
+  int out_dtype;      /* ATF_DTYPE_BF16 or ATF_DTYPE_F32 */
+  float* lse_out;     /* optional fp32 [B, Hq], natural log */
+  int* error_flag;
+} AtfDecodeParams;
+
+/* Paged-KV GQA split-KV decode followed by the LSE merge of its splits. */
+int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream);
+
+/* ------------------------------------------------------------------ merge */
+
+typedef struct {
+  const float* part_o;   /* ragged: [items, H, 128]; uniform: [P, B, H, 128] */
+  const float* part_lse; /* ragged: [items, H]; uniform: [P, B, H] */
+  const int32_t* part_indptr; /* device [B+1] for ragged parts; NULL for uniform P parts */
+  int32_t num_parts;     /* uniform case: P */
+  int32_t batch, num_heads, head_dim;
+  int lse_log2;          /* 1: part_lse in log2 domain, 0: natural log */
+  void* out;             /* [B, H, 128] */
+  int64_t o_stride_b, o_stride_h;
+  int out_dtype;         /* ATF_DTYPE_* */
+  float* lse_out;        /* optional [B, H], natural log */
+} AtfMergeParams;
+
+/* Merge partial attention states: LSE = log sum exp(LSE_i), O = sum exp(LSE_i - LSE) O_i. */
+int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream);
+
+/* ------------------------------------------------------------------ RoPE */
+
+typedef struct {
+  const void* x; /* bf16 [B, S, H, 128], pre-RoPE, rotate_half pair order */
+  void* out;     /* bf16 [B, S, H, 128] */
+  int64_t batch, seqlen, num_heads, head_dim;
+  int64_t x_stride_b, x_stride_s, x_stride_h;
+  int64_t o_stride_b, o_stride_s, o_stride_h;
+  const float* cos; /* fp32 [n_pos, 64]: row p = cos(p * inv_freq) */
+  const float* sin;
+  int64_t cs_stride_pos; /* elements between consecutive positions */
+  int64_t n_pos;
+  const int64_t* positions; /* optional device [S]; default pos_offset + s */
+  int64_t pos_offset;
+  int out_layout; /* ATF_LAYOUT_SORTED_PAIR or ATF_LAYOUT_ROTATE_HALF */
+} AtfRopeParams;
+
+/* rotate_half RoPE in fp32 (x1*cos - x2*sin, x2*cos + x1*sin, no FMA
+ * contraction), rounded to bf16, written in the requested pair order. */
+int atf_rope_pack(const AtfRopeParams* p, atf_stream_t stream);
+
+/* ------------------------------------------------------------------ misc */
+
+const char* atf_status_string(int status);
+int atf_version(void);
+/* Synchronises the current device, copies *error_flag to *out and clears it. */
+int atf_read_error_flag(int* error_flag_device, int* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATFLASH_B200_H_ */

@@ -1,0 +1,257 @@
+"""Paged decode parity on a B200 against the numpy oracle:
+ref_window_attn(phase="decode", block_m=1, block_n=1) for the 16-snap window
+(per-key levels) and ref_decode_sliced (gates/g2_correctness.py:43-70) for the
+vec8 window; window off == k=inf bitwise (gates/g1_bitexact.py analogue); split
+and KV-sharded runs merged by LSE equal the single run."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from _inputs import MAX_ABS_TOL, MEAN_ABS_TOL, err_stats, inv_sorted_perm, rope_tables, rope_hf_torch, sorted_perm
+from oracle import attention as OA
+from oracle import window_table as OWT
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def make_paged(kv_lens, hq, hkv, page_size, seed, layout="NHD", extra_pages=3):
+    """Random post-RoPE (sorted-pair) q and a paged KV cache with a seeded
+    permuted page table. Returns device tensors and per-request contiguous K/V."""
+    g = torch.Generator().manual_seed(seed)
+    npages = [(n + page_size - 1) // page_size for n in kv_lens]
+    total = sum(npages) + extra_pages
+    perm = torch.randperm(total, generator=g)
+    if layout == "NHD":
+        kc = torch.randn((total, page_size, hkv, 128), generator=g).to(torch.bfloat16)
+        vc = torch.randn((total, page_size, hkv, 128), generator=g).to(torch.bfloat16)
+    else:
+        kc = torch.randn((total, hkv, page_size, 128), generator=g).to(torch.bfloat16)
+        vc = torch.randn((total, hkv, page_size, 128), generator=g).to(torch.bfloat16)
+    q = torch.randn((len(kv_lens), hq, 128), generator=g).to(torch.bfloat16)
+    indptr = [0]
+    indices = []
+    c = 0
+    for n in npages:
+        indices += perm[c:c + n].tolist()
+        c += n
+        indptr.append(indptr[-1] + n)
+    lpl = [((n - 1) % page_size) + 1 for n in kv_lens]
+    ks, vs = [], []
+    for b, n in enumerate(kv_lens):
+        pages = indices[indptr[b]:indptr[b + 1]]
+        if layout == "NHD":
+            kb = kc[pages].reshape(-1, hkv, 128)[:n]
+            vb = vc[pages].reshape(-1, hkv, 128)[:n]
+        else:
+            kb = kc[pages].permute(0, 2, 1, 3).reshape(-1, hkv, 128)[:n]
+            vb = vc[pages].permute(0, 2, 1, 3).reshape(-1, hkv, 128)[:n]
+        ks.append(kb.permute(1, 0, 2).contiguous())  # (hkv, n, d)
+        vs.append(vb.permute(1, 0, 2).contiguous())
+    return (q, kc, vc, torch.tensor(indptr, dtype=torch.int32), torch.tensor(indices, dtype=torch.int32),
+            torch.tensor(lpl, dtype=torch.int32), ks, vs)
+
+
+def oracle_decode(q, ks, vs, base, k_ret):
+    w = OWT.wavelengths_sorted(128, base, float("inf") if k_ret is None else k_ret)
+    outs = []
+    for b in range(q.shape[0]):
+        o = OA.ref_window_attn(q[b][None, :, None, :].float().numpy(), ks[b][None].float().numpy(),
+                               vs[b][None].float().numpy(), w, phase="decode", block_m=1, block_n=1)
+        outs.append(o[0, :, 0, :])
+    return np.stack(outs)
+
+
+def run_decode(dev, q, kc, vc, indptr, indices, lpl, hq, hkv, page, layout="NHD", window_table=None,
+               window_mode="snap16", qk_layout="sorted_pair", max_chunk_keys=0, **runkw):
+    import atflash
+    ws = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout=layout)
+    w.plan(indptr, indices, lpl, hq, hkv, 128, page, window_table=window_table,
+           window_mode=window_mode, qk_layout=qk_layout, max_chunk_keys=max_chunk_keys)
+    res = w.run(q.to(dev), (kc.to(dev), vc.to(dev)), **runkw)
+    torch.cuda.synchronize()
+    assert atflash.check_device_errors() == 0
+    return res
+
+
+CASES = [
+    # (kv_lens, hq, hkv, page, layout, base, k_ret)
+    ([1000, 37, 513], 6, 2, 16, "NHD", 1e4, 2.0),
+    ([2048, 777], 24, 8, 16, "NHD", 5e5, 2.0),
+    ([3000], 28, 4, 64, "NHD", 1e7, 2.0),
+    ([1500, 64, 1], 28, 4, 64, "HND", 1e4, 1.0),
+    ([4096, 100], 8, 8, 16, "HND", 1e4, 3.0),
+    ([5000], 16, 1, 16, "NHD", 1e4, 2.0),
+]
+
+
+@pytest.mark.parametrize("window", ["on", "off"])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"L{'-'.join(map(str, c[0]))}-h{c[1]}x{c[2]}-p{c[3]}-{c[4]}")
+def test_decode_parity(cuda_device, case, window):
+    import atflash
+    kv_lens, hq, hkv, page, layout, base, k_ret = case
+    kr = k_ret if window == "on" else None
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, page, seed=sum(kv_lens) + hq,
+                                                        layout=layout)
+    wt = atflash.WindowTable(128, base, kr) if kr is not None else None
+    out = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, layout, wt)
+    ref = oracle_decode(q, ks, vs, base, kr)
+    mx, mean = err_stats(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
+
+
+def test_decode_many_splits_and_lse(cuda_device):
+    """Force 64-key items so a request spans dozens of splits; the merged output
+    and LSE match the oracle."""
+    import atflash
+    kv_lens, hq, hkv, page = [3000, 450], 6, 2, 16
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, page, seed=7)
+    wt = atflash.WindowTable(128, 1e4, 2.0)
+    out, lse = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", wt,
+                          max_chunk_keys=64, return_lse=True)
+    ref = oracle_decode(q, ks, vs, 1e4, 2.0)
+    mx, mean = err_stats(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+    # LSE of the windowed scores (natural log)
+    w = OWT.wavelengths_sorted(128, 1e4, 2.0)
+    for b in range(2):
+        _, lse_ref = OA.ref_window_attn(q[b][None, :, None, :].float().numpy(), ks[b][None].float().numpy(),
+                                        vs[b][None].float().numpy(), w, phase="decode", block_m=1,
+                                        block_n=1, return_lse=True)
+        assert np.abs(lse[b].cpu().numpy() - lse_ref[0, :, 0]).max() < 2e-3
+
+
+def test_decode_window_off_equals_kinf_bitwise(cuda_device):
+    import atflash
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged([2000, 300], 24, 8, 16, seed=9)
+    a = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, 24, 8, 16, "NHD", None)
+    b = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, 24, 8, 16, "NHD",
+                   atflash.WindowTable(128, 5e5, float("inf")))
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_decode_vec8_matches_g2_oracle(cuda_device):
+    """vec8 window (the FlashInfer port's 8-dim slices) vs ref_decode_sliced."""
+    import atflash
+    kv_lens, hq, hkv = [1000, 2500], 6, 2
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, 16, seed=13)
+    wt = atflash.WindowTable(128, 1e4, 2.0)
+    out = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, 16, "NHD", wt, window_mode="vec8")
+    zs = OWT.zhi_slice_vec8(128, 1e4, 2.0)
+    for b in range(2):
+        ref = OA.ref_decode_sliced(q[b].float().numpy(), ks[b].permute(1, 0, 2).float().numpy(),
+                                   vs[b].permute(1, 0, 2).float().numpy(), zs, 8)
+        mx, mean = err_stats(out[b].float().cpu().numpy(), ref)
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+
+
+def test_decode_against_golden(cuda_device):
+    """Kernel vs the reference's recorded decode outputs (contiguous KV as one-token pages)."""
+    import json
+    from _inputs import make_bhsd
+    import atflash
+    case = json.load(open(os.path.join(HERE, "golden", "attn_cases.json")))["decode"][0]
+    gold = np.load(os.path.join(HERE, "golden", f"attn_{case['name']}.npz"))
+    q, k, v, _ = make_bhsd(case["hq"], case["hkv"], case["N"], 128, case["base"], case["seed"], phase="decode")
+    N, hkv = case["N"], case["hkv"]
+    kc = k[0].permute(1, 0, 2).reshape(N, 1, hkv, 128).contiguous()  # page_size 1, NHD
+    vc = v[0].permute(1, 0, 2).reshape(N, 1, hkv, 128).contiguous()
+    indptr = torch.tensor([0, N], dtype=torch.int32)
+    indices = torch.arange(N, dtype=torch.int32)
+    lpl = torch.tensor([1], dtype=torch.int32)
+    for kr in case["k_rets"]:
+        tag = "inf" if kr == "inf" else f"{kr:g}"
+        wt = None if kr == "inf" else atflash.WindowTable(128, case["base"], float(kr))
+        out = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, 1,
+                         "NHD", wt)
+        mx, mean = err_stats(out[0].float().cpu().numpy(), gold[f"out32_k{tag}"][0, :, 0])
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+        if wt is not None:
+            out8 = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, 1,
+                              "NHD", wt, window_mode="vec8")
+            mx, mean = err_stats(out8[0].float().cpu().numpy(), gold[f"vec8_k{tag}"])
+            assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+
+
+def test_decode_rotate_half_cache(cuda_device):
+    """A cache holding K in HF rotate_half order (and q likewise) gives the
+    sorted-layout result."""
+    import atflash
+    kv_lens, hq, hkv = [1200, 90], 6, 2
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, 16, seed=17)
+    inv = inv_sorted_perm(128)
+    wt = atflash.WindowTable(128, 1e4, 2.0)
+    a = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, 16, "NHD", wt)
+    b = run_decode(cuda_device, q[..., inv].contiguous(), kc[..., inv].contiguous(), vc, indptr, indices, lpl,
+                   hq, hkv, 16, "NHD", wt, qk_layout="rotate_half")
+    assert (a.float() - b.float()).abs().max().item() < 2e-3
+
+
+def test_kv_sharded_decode_merge(cuda_device):
+    """Two KV shards with global positions (kv_pos0) merged by LSE equal the full
+    decode: the single-GPU emulation of atflash.dist.sharded_decode."""
+    import atflash
+    N, hq, hkv, page = 4096, 28, 4, 64
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged([N], hq, hkv, page, seed=23)
+    wt = atflash.WindowTable(128, 1e7, 64.0)
+    full = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", wt)
+    pages = indices.tolist()
+    parts_o, parts_l = [], []
+    for r, (p0, p1) in enumerate([(0, 24), (24, 64)]):
+        sub_idx = torch.tensor(pages[p0:p1], dtype=torch.int32)
+        o, l = run_decode(cuda_device, q, kc, vc, torch.tensor([0, p1 - p0], dtype=torch.int32), sub_idx,
+                          torch.tensor([page], dtype=torch.int32), hq, hkv, page, "NHD", wt,
+                          q_pos=torch.tensor([N - 1]), kv_pos0=torch.tensor([p0 * page]),
+                          return_lse=True, out_dtype=torch.float32)
+        parts_o.append(o)
+        parts_l.append(l)
+    merged = atflash.lse_merge(torch.stack(parts_o), torch.stack(parts_l))
+    torch.cuda.synchronize()
+    assert (merged.float() - full.float()).abs().max().item() < 4e-3
+    ref = oracle_decode(q, ks, vs, 1e7, 64.0)
+    mx, mean = err_stats(merged.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+
+
+def test_rope_pack_bit_exact(cuda_device):
+    """Fused RoPE + pack equals the reference front-end (fp32 rotate_half RoPE,
+    permutation, bf16) bit for bit given the same cos/sin tables."""
+    import atflash
+    g = torch.Generator().manual_seed(3)
+    B, S, H = 2, 333, 5
+    x = torch.randn((B, S, H, 128), generator=g).to(torch.bfloat16)
+    cos, sin = rope_tables(S + 50, 128, 5e5)
+    for off in (0, 50):
+        c, s_ = cos[off:off + S][None, :, None, :], sin[off:off + S][None, :, None, :]
+        ref_rh = rope_hf_torch(x, c, s_).to(torch.bfloat16)
+        ref_sp = rope_hf_torch(x, c, s_)[..., sorted_perm(128)].to(torch.bfloat16)
+        got_rh = atflash.rope_pack(x.to(cuda_device), cos.to(cuda_device), sin.to(cuda_device), pos_offset=off,
+                                   out_layout="rotate_half")
+        got_sp = atflash.rope_pack(x.to(cuda_device), cos.to(cuda_device), sin.to(cuda_device), pos_offset=off,
+                                   out_layout="sorted_pair")
+        torch.cuda.synchronize()
+        assert torch.equal(got_rh.cpu().view(torch.int16), ref_rh.view(torch.int16))
+        assert torch.equal(got_sp.cpu().view(torch.int16), ref_sp.view(torch.int16))
+
+
+def test_prefill_with_rope_end_to_end(cuda_device):
+    """flash_attn_func(rope=(cos, sin)) on pre-RoPE HF tensors equals the oracle on
+    the reference front-end's post-RoPE sorted tensors."""
+    import atflash
+    from _inputs import make_bhsd
+    q, k, v, (q0, k0, cos, sin) = make_bhsd(6, 2, 640, 128, 5e5, 29)
+    dev = cuda_device
+    out = atflash.flash_attn_func(q0.transpose(1, 2).contiguous().to(dev), k0.transpose(1, 2).contiguous().to(dev),
+                                  v.transpose(1, 2).contiguous().to(dev), causal=True,
+                                  window_table=atflash.WindowTable(128, 5e5, 2.0),
+                                  rope=(cos.to(dev), sin.to(dev)))
+    torch.cuda.synchronize()
+    w = OWT.wavelengths_sorted(128, 5e5, 2.0)
+    ref = OA.ref_window_attn(q.float().numpy(), k.float().numpy(), v.float().numpy(), w, phase="prefill",
+                             block_m=128, block_n=128)
+    mx, mean = err_stats(out.transpose(1, 2).float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL

@@ -1,0 +1,125 @@
+"""CPU checks of the C ABI library: it loads, exports every function
+include/atflash_b200.h declares, rejects bad arguments before touching a GPU,
+and its host-side split-KV planner covers every key exactly once."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+HEADER = os.path.join(ROOT, "include", "atflash_b200.h")
+
+
+def _lib():
+    from atflash import _ffi
+    try:
+        return _ffi.load()
+    except (ImportError, OSError) as e:
+        pytest.skip(f"library not built: {e}")
+
+
+def declared_functions():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(atf_\w+)\(", txt, flags=re.M)))
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    for n in ("atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_lse_merge",
+              "atf_status_string", "atf_rope_pack", "atf_window_zhi16"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    from atflash import _ffi
+    assert set(_ffi.EXPORTED) >= set(declared_functions())
+
+
+def test_status_strings():
+    from atflash import _ffi
+    _lib()
+    assert _ffi.status_string(0) == "ok"
+    assert "argument" in _ffi.status_string(-1)
+    assert _ffi.status_string(-99) == "unknown status"
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    from atflash import _ffi
+    lib = _lib()
+    assert lib.atf_prefill_fwd(None, None) == -1
+    p = _ffi.AtfPrefillParams()
+    assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -1  # null tensors
+    p.q = p.k = p.v = p.out = 16
+    p.head_dim = 64
+    assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -2  # head_dim 64 unsupported
+    p.head_dim = 128
+    p.batch = p.seqlen_q = p.seqlen_k = 1
+    p.num_heads_q, p.num_heads_kv = 6, 4
+    assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -1  # heads not a multiple
+    p.num_heads_kv = 2
+    p.softmax_scale = 0.1
+    p.q = 17
+    assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -3  # misaligned
+    assert lib.atf_decode_run(None, None) == -1
+    assert lib.atf_lse_merge(None, None) == -1
+    assert lib.atf_rope_pack(None, None) == -1
+    r = _ffi.AtfRopeParams()
+    r.x, r.out, r.cos, r.sin = 16, 16, 32, 48
+    r.head_dim, r.n_pos, r.cs_stride_pos = 128, 1, 64
+    assert lib.atf_rope_pack(ctypes.byref(r), None) == -1  # in place
+
+
+def _plan(lib, lens, page, hq=24, hkv=8, **kw):
+    from atflash import _ffi
+    npages = [(n + page - 1) // page for n in lens]
+    indptr = np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)
+    lpl = np.array([((n - 1) % page) + 1 for n in lens], dtype=np.int32)
+    pp = _ffi.AtfDecodePlanParams()
+    pp.batch_size, pp.num_qo_heads, pp.num_kv_heads, pp.head_dim, pp.page_size = len(lens), hq, hkv, 128, page
+    pp.indptr_host, pp.last_page_len_host = indptr.ctypes.data, lpl.ctypes.data
+    pp.num_sms = kw.get("sms", 148)
+    pp.max_chunk_keys = kw.get("max_chunk", 0)
+    plan = _ffi.AtfDecodePlan()
+    assert lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)) == 0
+    items = np.zeros((max(1, plan.num_items), 4), dtype=np.int32)
+    iptr = np.zeros(len(lens) + 1, dtype=np.int32)
+    P32 = ctypes.POINTER(ctypes.c_int32)
+    assert lib.atf_decode_plan(ctypes.byref(pp), items.ctypes.data_as(P32), items.shape[0],
+                               iptr.ctypes.data_as(P32), ctypes.byref(plan)) == 0
+    return plan, items[:plan.num_items], iptr
+
+
+@pytest.mark.parametrize("lens,page", [([131072] * 8, 16), ([8192, 1, 70000], 16), ([1048576], 64), ([5], 1)])
+def test_decode_plan_covers_every_key_once(lens, page):
+    lib = _lib()
+    plan, items, iptr = _plan(lib, lens, page)
+    assert plan.chunk_keys % 64 == 0
+    for b, n in enumerate(lens):
+        its = items[iptr[b]:iptr[b + 1]]
+        assert its[:, 0].tolist() == [b] * len(its)
+        cover = np.zeros(n, dtype=np.int32)
+        for (_, k0, k1, _) in its:
+            cover[k0:k1] += 1
+        assert (cover == 1).all()
+    assert plan.partial_o_floats == plan.num_items * 24 * 128
+
+
+def test_decode_plan_rejects_bad_tables():
+    from atflash import _ffi
+    lib = _lib()
+    indptr = np.array([0, 2], dtype=np.int32)
+    lpl = np.array([17], dtype=np.int32)  # > page size
+    pp = _ffi.AtfDecodePlanParams()
+    pp.batch_size, pp.num_qo_heads, pp.num_kv_heads, pp.head_dim, pp.page_size = 1, 8, 8, 128, 16
+    pp.indptr_host, pp.last_page_len_host = indptr.ctypes.data, lpl.ctypes.data
+    plan = _ffi.AtfDecodePlan()
+    assert lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)) == -1
+    pp.num_qo_heads = 8 * 17  # group of 17 > 16
+    lpl[0] = 3
+    assert lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)) == -2
