@@ -216,11 +216,11 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def bench_decode(device, steps, warmup, peaks):
+def bench_decode(device, steps, warmup, peaks, N=131072):
     """BASELINE config 3 at 128K: batch 8, 24/8 heads, page 16, theta 5e5, k=2 vs off."""
     import atflash
     from atflash import window_table as WT
-    B, hq, hkv, page, N = 8, 24, 8, 16, 131072
+    B, hq, hkv, page = 8, 24, 8, 16
     npg = N // page
     total = B * npg
     g = torch.Generator(device="cpu").manual_seed(1234 + N + D)
@@ -255,7 +255,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="atflash", choices=["atflash", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip off/k64/decode/e2e/cpu legs")
+    ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
+                    help="prefill: the headline leg alone; decode: the config-3 decode leg alone")
+    ap.add_argument("--seq-len", type=int, default=131072,
+                    help="sequence length (smaller values are for profiling captures)")
     args = ap.parse_args()
+    global N_CTX
+    N_CTX = args.seq_len
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         # CPU arm: rank 0 alone times the oracle port; other ranks exit without work
@@ -266,6 +272,11 @@ def main():
     from atflash import window_table as WT
     device = torch.device("cuda", local)
     peaks = load_peaks()
+    if args.only == "decode":
+        res = bench_decode(device, args.steps, args.warmup, peaks, N=args.seq_len)
+        if rank == 0:
+            print(json.dumps({"decode": res}), flush=True)
+        return
     inputs = prefill_inputs(device)
     wt2 = atflash.WindowTable(D, THETA, K_RET)
     blocks = atflash.dist.zigzag_blocks(N_CTX, world, rank) if world > 1 else [(0, N_CTX)]
@@ -326,12 +337,12 @@ def main():
         e2e = {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         del qd, kd, vd
     decode = None
-    if not args.no_extras and rank == 0 and world == 1:
+    if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
         del inputs
         torch.cuda.empty_cache()
         decode = bench_decode(device, 20, 5, peaks)
     cpu = None
-    if not args.no_extras and rank == 0 and world == 1:
+    if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
         cms, info = cpu_baseline_sample()
         cpu = dict(info, value=cms, unit="ms")
     if rank == 0:
