@@ -1,33 +1,43 @@
 // Windowed causal prefill for sm_100a: warp-specialised tcgen05 / TMEM kernel.
 //
 // One CTA owns two 128-row query tiles (Q0, Q1) of one (batch, q head) and
-// streams the key/value tiles (128 keys) of its causal range:
+// streams 128-key K/V tiles over its causal range:
 //
 //   warp 8       TMA producer. Q once (8 levels x 2 halves per tile); per key
 //                tile only the in-window K levels (L = D_eff/16 of the nearer
-//                query tile) and both 64-dim V boxes.
-//   warp 9       MMA issuer (one lane) and TMEM owner (512 columns):
-//                S_t = Q_t K^T over L(t, j) K-steps of 16 dims into TMEM,
-//                O_t += P_t V with P_t read from TMEM (bf16, aliased on S_t).
+//                query tile) and the two 64-dim V boxes.
+//   warp 9       MMA issuer and TMEM owner (512 columns). For key tile j:
+//                O_0 += P_0(j) V_j, S_0(j+1) = Q_0 K_{j+1}^T, then the same for
+//                Q1, so each query tile's softmax overlaps the other tile's MMAs.
+//                S_t is computed over L(t, j) K-steps of 16 dims; P_t (bf16) is
+//                written back into the first 64 columns of S_t and read by the
+//                O += P V MMA straight from TMEM.
 //   warps 0-3/4-7  softmax for Q0 / Q1: one query row per thread, online
-//                softmax in the log2 domain, conditional O rescale, epilogue.
+//                softmax in the log2 domain, lazy O rescale, epilogue.
+//
+// Issue discipline: the producer and MMA warps run their schedules with all 32
+// lanes and warp-uniform operands (TMEM base broadcast, descriptors built once
+// and advanced by adds); one elected lane issues each TMA / tcgen05.mma /
+// tcgen05.commit. 128-column MMAs issued this way run at the tensor pipe's
+// peak; a lane-0-only branch costs several times more per instruction.
 //
 // The window is the reference's tile quantisation (atflash/reference.py:59-68,
-// atflash/window_table.py:70-76): for query tile q0 and key tile n0 the QK
-// contraction runs over D_eff(z_min) dims with z_min = max(0, q0 - (n0+127));
-// D_eff(z) = 16 * #{i : zhi[i] >= z} (window_tables/atflash_window.py:85-108).
-// The causal diagonal and ragged tails use per-element predicates.
+// atflash/window_table.py:70-76) at block_m = block_n = 128: for query tile q0
+// and key tile n0 the QK contraction runs over D_eff(z_min) dims with
+// z_min = max(0, q0 - (n0+127)); D_eff(z) = 16 * #{i : zhi[i] >= z}
+// (window_tables/atflash_window.py:85-108). The causal diagonal and ragged
+// tails use per-element predicates.
 //
 // Shared memory (1024-aligned):
 //   Q  2 tiles x 8 level slabs x 4 KB. A slab is the canonical no-swizzle
-//      K-major layout: two 2 KB halves (dims 0-7 and 8-15 of the level), each
+//      K-major layout: two halves (dims 0-7 and 8-15 of the level), each
 //      128 rows x 16 B, so core matrices (8 rows x 16 B) are contiguous:
-//      LBO (K direction) = 2048 B, SBO (8-row groups) = 128 B.
+//      LBO (K direction) = 2 KB, SBO (8-row groups) = 128 B.
 //   K  2 stages x 8 slabs x 4 KB, same layout.
 //   V  2 stages x 2 boxes (dims 0-63, 64-127) x 128 keys x 128 B, 128B swizzle;
 //      the PV B operand is MN-major: LBO (next 64 dims) = 16 KB, SBO (next 8
 //      keys) = 1 KB.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// TMEM columns: S_t at 128t, O_t at 256 + 128t.
 #include <math.h>
 
 #include "atf_internal.h"
@@ -38,12 +48,14 @@ namespace prefill {
 
 constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
 constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
-constexpr uint32_t HALF_BYTES = 2048;
-constexpr uint32_t SLAB_BYTES = 2 * HALF_BYTES;
-constexpr uint32_t QTILE_BYTES = 8 * SLAB_BYTES;
-constexpr uint32_t KSTAGE_BYTES = 8 * SLAB_BYTES;
-constexpr uint32_t VBOX_BYTES = BN * 128;
-constexpr uint32_t VSTAGE_BYTES = 2 * VBOX_BYTES;
+constexpr uint32_t QHALF_BYTES = BM * 16;             // 2 KB
+constexpr uint32_t QSLAB_BYTES = 2 * QHALF_BYTES;     // 4 KB
+constexpr uint32_t QTILE_BYTES = 8 * QSLAB_BYTES;     // 32 KB
+constexpr uint32_t KHALF_BYTES = BN * 16;             // 2 KB
+constexpr uint32_t KSLAB_BYTES = 2 * KHALF_BYTES;     // 4 KB
+constexpr uint32_t KSTAGE_BYTES = 8 * KSLAB_BYTES;    // 32 KB
+constexpr uint32_t VBOX_BYTES = BN * 128;             // 16 KB
+constexpr uint32_t VSTAGE_BYTES = 2 * VBOX_BYTES;     // 32 KB
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = OFF_Q + NQ * QTILE_BYTES;
 constexpr uint32_t OFF_V = OFF_K + KST * KSTAGE_BYTES;
@@ -55,10 +67,11 @@ enum {
   B_KEMPTY = B_KFULL + KST,
   B_VFULL = B_KEMPTY + KST,
   B_VEMPTY = B_VFULL + VST,
-  B_SFULL = B_VEMPTY + VST,
-  B_PFULL = B_SFULL + NQ,
-  B_ODONE = B_PFULL + NQ,
-  B_FINAL = B_ODONE + NQ,
+  B_SFULL = B_VEMPTY + VST,   // [t]
+  B_PFULL = B_SFULL + NQ,     // [t]
+  B_ODONE = B_PFULL + NQ,     // [t], one phase per O += P V
+  B_OFINAL = B_ODONE + NQ,    // [t], single phase: the tile's last O += P V done
+  B_FINAL = B_OFINAL + NQ,
   NUM_BARS
 };
 constexpr uint32_t OFF_ABORT = OFF_BAR + 8 * NUM_BARS;
@@ -66,8 +79,8 @@ constexpr uint32_t OFF_TMEM = OFF_ABORT + 16;
 constexpr uint32_t SMEM_USED = OFF_TMEM + 16;
 constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // slack for 1024-B alignment
 
-constexpr uint32_t IDESC_QK = make_idesc_bf16(128, 128, 0, 0);
-constexpr uint32_t IDESC_PV = make_idesc_bf16(128, 128, 0, 1);
+constexpr uint32_t IDESC_QK = make_idesc_bf16(128, BN, 0, 0);
+constexpr uint32_t IDESC_PV = make_idesc_bf16(128, HD, 0, 1);
 constexpr uint32_t FULL = 0xffffffffu;
 
 struct Args {
@@ -164,6 +177,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar(B_SFULL + t), 1);
       mbar_init(bar(B_PFULL + t), 128);
       mbar_init(bar(B_ODONE + t), 1);
+      mbar_init(bar(B_OFINAL + t), 1);
     }
     mbar_init(bar(B_FINAL), 1);
     fence_mbar_init();
@@ -186,50 +200,53 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (start_ok && warp == WARP_LOAD) {
     // ---------------------------------------------------------------- producer
+    // All 32 lanes run this loop with warp-uniform values; one elected lane
+    // issues each TMA / expect_tx.
     int issued_k = 0, issued_v = 0;
     bool ok = true;
-    if (lane == 0) {
+    {
       uint32_t qbytes = 0;
 #pragma unroll
       for (int t = 0; t < NQ; ++t) qbytes += nk[t] > 0 ? QTILE_BYTES : 0u;
-      mbar_arrive_expect_tx(bar(B_Q), qbytes);
+      mbar_arrive_expect_tx_elect(bar(B_Q), qbytes);
+#pragma unroll
       for (int t = 0; t < NQ; ++t) {
         if (nk[t] == 0) continue;
+#pragma unroll
         for (int i = 0; i < 8; ++i)
+#pragma unroll
           for (int hh = 0; hh < 2; ++hh)
-            tma_load_4d(sb + OFF_Q + t * QTILE_BYTES + i * SLAB_BYTES + hh * HALF_BYTES, &tmQ,
-                        bar(B_Q), level_col(a.layout, i, hh), row0[t], h, bi);
+            tma_load_4d_elect(sb + OFF_Q + t * QTILE_BYTES + i * QSLAB_BYTES + hh * QHALF_BYTES, &tmQ,
+                              bar(B_Q), level_col(a.layout, i, hh), row0[t], h, bi);
       }
     }
     for (int j = 0; j < nk_max; ++j) {
       const int ks = j % KST, vs = j % VST;
       ok = __all_sync(FULL, mbar_wait(bar(B_KEMPTY + ks), ((j / KST) & 1) ^ 1, ab, kDevErrTimeout));
       if (!ok) break;
-      if (lane == 0) {
-        int L = 0;
-        for (int t = 0; t < NQ; ++t)
-          if (j < nk[t]) {
-            const int lt = levels_for(a, row0[t], j);
-            L = lt > L ? lt : L;
-          }
-        mbar_arrive_expect_tx(bar(B_KFULL + ks), static_cast<uint32_t>(L) * SLAB_BYTES);
-        for (int i = 0; i < L; ++i)
-          for (int hh = 0; hh < 2; ++hh)
-            tma_load_4d(sb + OFF_K + ks * KSTAGE_BYTES + i * SLAB_BYTES + hh * HALF_BYTES, &tmK,
-                        bar(B_KFULL + ks), level_col(a.layout, i, hh), j * BN, hk, bi);
+      int L = 0;
+#pragma unroll
+      for (int t = 0; t < NQ; ++t)
+        if (j < nk[t]) {
+          const int lt = levels_for(a, row0[t], j);
+          L = lt > L ? lt : L;
+        }
+      mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
+      const uint32_t kdst = sb + OFF_K + ks * KSTAGE_BYTES;
+      for (int i = 0; i < L; ++i) {
+        tma_load_4d_elect(kdst + i * KSLAB_BYTES, &tmK, bar(B_KFULL + ks), level_col(a.layout, i, 0),
+                          j * BN, hk, bi);
+        tma_load_4d_elect(kdst + i * KSLAB_BYTES + KHALF_BYTES, &tmK, bar(B_KFULL + ks),
+                          level_col(a.layout, i, 1), j * BN, hk, bi);
       }
       issued_k = j + 1;
-      __syncwarp();
       ok = __all_sync(FULL, mbar_wait(bar(B_VEMPTY + vs), ((j / VST) & 1) ^ 1, ab, kDevErrTimeout));
       if (!ok) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar(B_VFULL + vs), VSTAGE_BYTES);
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(sb + OFF_V + vs * VSTAGE_BYTES + c * VBOX_BYTES, &tmV, bar(B_VFULL + vs),
-                      64 * c, j * BN, hk, bi);
-      }
+      mbar_arrive_expect_tx_elect(bar(B_VFULL + vs), VSTAGE_BYTES);
+      tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES, &tmV, bar(B_VFULL + vs), 0, j * BN, hk, bi);
+      tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES + VBOX_BYTES, &tmV, bar(B_VFULL + vs), 64,
+                        j * BN, hk, bi);
       issued_v = j + 1;
-      __syncwarp();
     }
     // Drain: every copy this warp issued must land before shared memory is
     // released (no-op on the normal path, where the MMA warp consumed them).
@@ -241,43 +258,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
   } else if (start_ok && warp == WARP_MMA) {
     // ---------------------------------------------------------------- MMA issuer
-    const uint32_t qbase = sb + OFF_Q, kbase = sb + OFF_K, vbase = sb + OFF_V;
+    // Descriptors are built once and advanced by adding (byte offset >> 4) to
+    // the start-address field (all offsets stay inside the 14-bit field).
+    const uint32_t tm = __shfl_sync(FULL, tmem, 0);
+    const uint64_t qdesc0 = make_sdesc(sb + OFF_Q, QHALF_BYTES, 128, kLayoutNone);
+    const uint64_t kdesc0 = make_sdesc(sb + OFF_K, KHALF_BYTES, 128, kLayoutNone);
+    const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
     auto issue_S = [&](int t, int j) {
-      const int ks = j % KST;
       const int L = levels_for(a, row0[t], j);
-      const uint32_t d_tmem = tmem + static_cast<uint32_t>(t * 128);
-      for (int i = 0; i < L; ++i) {
-        const uint64_t ad = make_sdesc(qbase + t * QTILE_BYTES + i * SLAB_BYTES, HALF_BYTES, 128,
-                                       kLayoutNone);
-        const uint64_t bd = make_sdesc(kbase + ks * KSTAGE_BYTES + i * SLAB_BYTES, HALF_BYTES, 128,
-                                       kLayoutNone);
-        mma_ss(d_tmem, ad, bd, IDESC_QK, i > 0 ? 1u : 0u);
-      }
-      tc_commit(bar(B_SFULL + t));
+      const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
+      const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
+      const uint64_t kd = kdesc0 + (((j % KST) * KSTAGE_BYTES) >> 4);
+      for (int i = 0; i < L; ++i)
+        mma_ss_elect(d_tmem, qd + ((i * QSLAB_BYTES) >> 4), kd + ((i * KSLAB_BYTES) >> 4), IDESC_QK,
+                     i > 0 ? 1u : 0u);
+      tc_commit_elect(bar(B_SFULL + t));
     };
     auto issue_PV = [&](int t, int j) {
-      const int vs = j % VST;
-      const uint32_t o_tmem = tmem + 256u + static_cast<uint32_t>(t * 128);
-      const uint32_t p_tmem = tmem + static_cast<uint32_t>(t * 128);
-      for (int c = 0; c < BN / 16; ++c) {
-        const uint64_t bd =
-            make_sdesc(vbase + vs * VSTAGE_BYTES + c * 2048, VBOX_BYTES, 1024, kLayoutSw128);
-        mma_ts(o_tmem, p_tmem + static_cast<uint32_t>(c * 8), bd, IDESC_PV,
-               (j > 0 || c > 0) ? 1u : 0u);
-      }
-      tc_commit(bar(B_ODONE + t));
+      const uint32_t o_tmem = tm + 256u + static_cast<uint32_t>(t * 128);
+      const uint32_t p_tmem = tm + static_cast<uint32_t>(t * 128);
+      const uint64_t vd = vdesc0 + (((j % VST) * VSTAGE_BYTES) >> 4);
+#pragma unroll
+      for (int c = 0; c < BN / 16; ++c)
+        mma_ts_elect(o_tmem, p_tmem + static_cast<uint32_t>(c * 8), vd + ((c * 2048) >> 4), IDESC_PV,
+                     (j > 0 || c > 0) ? 1u : 0u);
+      tc_commit_elect(bar(B_ODONE + t));
     };
     bool ok = __all_sync(FULL, mbar_wait(bar(B_Q), 0, ab, kDevErrTimeout));
     tc_fence_after();
     if (ok && nk_max > 0) {
       ok = __all_sync(FULL, mbar_wait(bar(B_KFULL + 0), 0, ab, kDevErrTimeout));
       tc_fence_after();
-      if (ok && lane == 0) {
+      if (ok) {
+#pragma unroll
         for (int t = 0; t < NQ; ++t)
           if (nk[t] > 0) issue_S(t, 0);
-        tc_commit(bar(B_KEMPTY + 0));
+        tc_commit_elect(bar(B_KEMPTY + 0));
       }
-      __syncwarp();
     }
     for (int j = 0; ok && j < nk_max; ++j) {
       const int vs = j % VST;
@@ -292,8 +309,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + t), j & 1, ab, kDevErrTimeout));
           if (!ok) break;
           tc_fence_after();
-          if (lane == 0) issue_PV(t, j);
-          __syncwarp();
+          issue_PV(t, j);
+          if (j + 1 == nk[t]) tc_commit_elect(bar(B_OFINAL + t));
         }
         if (j + 1 < nk[t]) {
           if (!kwaited) {
@@ -304,19 +321,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             kwaited = true;
           }
-          if (lane == 0) issue_S(t, j + 1);
-          __syncwarp();
+          // S_t(j+1) overwrites the TMEM columns P_t(j) occupies; the O += P V
+          // above was issued first and tcgen05.mma ops of one thread run in order.
+          issue_S(t, j + 1);
         }
       }
       if (!ok) break;
-      if (lane == 0) {
-        if (kwaited) tc_commit(bar(B_KEMPTY + (j + 1) % KST));
-        tc_commit(bar(B_VEMPTY + vs));
-      }
-      __syncwarp();
+      if (kwaited) tc_commit_elect(bar(B_KEMPTY + (j + 1) % KST));
+      tc_commit_elect(bar(B_VEMPTY + vs));
     }
     // Every MMA issued by this CTA completes before TMEM is released.
-    if (lane == 0) tc_commit(bar(B_FINAL));
+    tc_commit_elect(bar(B_FINAL));
     __syncwarp();
     drain_wait(bar(B_FINAL), 0);
     __syncwarp();
@@ -340,12 +355,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       float s[BN];
+      {
+        uint32_t rr[BN];
+        tmem_ld128(tS, rr);
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
-        uint32_t rr[32];
-        tmem_ld32(tS + static_cast<uint32_t>(32 * c4), rr);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[32 * c4 + e] = __uint_as_float(rr[e]);
+        for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
       }
       if (needs_mask(a, my_row0, j)) {
         const long long n0 = static_cast<long long>(j) * BN;
@@ -381,29 +395,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const float msub = (m2 == -INFINITY) ? 0.f : m2;
       float ls0 = 0.f, ls1 = 0.f;
-      uint32_t pk0[32], pk1[32];
+      uint32_t pk[BN / 2];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < BN / 2; ++c) {
         const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -msub));
         const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
         ls0 += p0;
         ls1 += p1;
-        pk0[c] = pack_bf16x2(p0, p1);
-      }
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float p0 = ex2_approx(fmaf(s[64 + 2 * c], sl2, -msub));
-        const float p1 = ex2_approx(fmaf(s[64 + 2 * c + 1], sl2, -msub));
-        ls0 += p0;
-        ls1 += p1;
-        pk1[c] = pack_bf16x2(p0, p1);
+        pk[c] = pack_bf16x2(p0, p1);
       }
       l += ls0 + ls1;
-      tmem_st32(tS, pk0);
-      tmem_st32(tS + 32u, pk1);
+      tmem_st64(tS, pk);
       if (__any_sync(FULL, need)) {
-        // O holds the sum up to tile j-1 once PV(t, j-1) has completed; PV(t, j)
-        // is not issued before this warpgroup arrives on PFULL below.
+        // O holds the sum up to tile j-1 once PV(t, j-1) has completed (S_t(j) was
+        // issued after it, so at most that one is in flight); PV(t, j) is not
+        // issued before this warpgroup arrives on PFULL below.
         ok = __all_sync(FULL, mbar_wait(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout));
         if (!ok) break;
         tc_fence_after();
@@ -420,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(bar(B_PFULL + t));
     }
     if (ok && my_nk > 0) {
-      ok = __all_sync(FULL, mbar_wait(bar(B_ODONE + t), (my_nk - 1) & 1, ab, kDevErrTimeout));
+      ok = __all_sync(FULL, mbar_wait(bar(B_OFINAL + t), 0, ab, kDevErrTimeout));
       if (ok) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.0f / l : 0.f;
@@ -504,7 +510,7 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     const uint64_t dims[4] = {128, (uint64_t)p->seqlen_q, (uint64_t)p->num_heads_q, (uint64_t)p->batch};
     const uint64_t str[3] = {sane(p->q_stride_s, p->seqlen_q), sane(p->q_stride_h, p->num_heads_q),
                              sane(p->q_stride_b, p->batch)};
-    const uint32_t box[4] = {8, BM, 1, 1};
+    const uint32_t box[4] = {8, static_cast<uint32_t>(BM), 1, 1};
     if ((rc = encode_tiled_bf16(&tq, p->q, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != ATF_OK)
       return rc;
   }
@@ -512,7 +518,7 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     const uint64_t dims[4] = {128, (uint64_t)p->seqlen_k, (uint64_t)p->num_heads_kv, (uint64_t)p->batch};
     const uint64_t str[3] = {sane(p->k_stride_s, p->seqlen_k), sane(p->k_stride_h, p->num_heads_kv),
                              sane(p->k_stride_b, p->batch)};
-    const uint32_t box[4] = {8, BN, 1, 1};
+    const uint32_t box[4] = {8, static_cast<uint32_t>(BN), 1, 1};
     if ((rc = encode_tiled_bf16(&tk, p->k, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != ATF_OK)
       return rc;
   }
@@ -520,7 +526,7 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     const uint64_t dims[4] = {128, (uint64_t)p->seqlen_k, (uint64_t)p->num_heads_kv, (uint64_t)p->batch};
     const uint64_t str[3] = {sane(p->v_stride_s, p->seqlen_k), sane(p->v_stride_h, p->num_heads_kv),
                              sane(p->v_stride_b, p->batch)};
-    const uint32_t box[4] = {64, BN, 1, 1};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(BN), 1, 1};
     if ((rc = encode_tiled_bf16(&tv, p->v, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
       return rc;
   }

@@ -41,7 +41,7 @@ K_RETS = (1.0, 1.5, 2.0, 3.0, 4.0, 64.0, float("inf"))
 HEAD_DIMS = (64, 128)
 CAPS = (8192, 131072, 1_100_000)
 
-# (name, hq, hkv, N, base, k_ret list, seed) -- prefill cases (block 128 x 128)
+# (name, hq, hkv, N, base, k_ret list, seed) -- prefill cases at the kernel tile (block 128 x 128)
 PREFILL_CASES = [
     ("prefill_g3", 3, 1, 448, 1e4, (2.0, float("inf")), 777),
     ("prefill_g7", 7, 1, 320, 1e4, (1.0,), 778),

@@ -20,6 +20,7 @@ from oracle import window_table as OWT
 
 pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
+BM, BN = 128, 128  # the kernel's tile; the window is quantised per (query tile, key tile)
 
 
 def _atf():
@@ -46,8 +47,8 @@ def _run(q, k, v, dev, base, k_ret, layout="sorted_pair", **kw):
 
 def _oracle(q, k, v, base, k_ret, mode="fp32", **kw):
     w = OWT.wavelengths_sorted(128, base, float("inf") if k_ret is None else k_ret)
-    return OA.ref_window_attn(to_np(q), to_np(k), to_np(v), w, phase="prefill", block_m=128,
-                              block_n=128, mode=mode, **kw)
+    return OA.ref_window_attn(to_np(q), to_np(k), to_np(v), w, phase="prefill", block_m=BM,
+                              block_n=BN, mode=mode, **kw)
 
 
 CASES = [
@@ -188,7 +189,7 @@ def test_prefill_lse(cuda_device):
     q, k, v, _ = make_bhsd(6, 2, 500, 128, 1e4, 61)
     w = OWT.wavelengths_sorted(128, 1e4, 2.0)
     ref, lse_ref = OA.ref_window_attn(to_np(q), to_np(k), to_np(v), w, phase="prefill", block_m=128,
-                                      block_n=128, return_lse=True)
+                                      block_n=BN, return_lse=True)
     out, lse = atflash.prefill_fwd(_bshd(q, cuda_device), _bshd(k, cuda_device), _bshd(v, cuda_device),
                                    window_table=atflash.WindowTable(128, 1e4, 2.0), return_lse=True)
     torch.cuda.synchronize()
@@ -232,7 +233,7 @@ def test_prefill_full_size_sampled_tiles(cuda_device):
             qn = q[:, t * 128:hi, h:h + 1].transpose(1, 2).float().cpu().numpy()
             kn = k[:, :hi, hk:hk + 1].transpose(1, 2).float().cpu().numpy()
             vn = v[:, :hi, hk:hk + 1].transpose(1, 2).float().cpu().numpy()
-            ref = OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=128, block_n=128,
+            ref = OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=BM, block_n=BN,
                                      q_offset=t * 128)
             got = out[:, t * 128:hi, h:h + 1].transpose(1, 2).float().cpu().numpy()
             mx, mean = err_stats(got, ref)
