@@ -52,7 +52,7 @@ class AtfDecodePlan(ctypes.Structure):
 
 class AtfDecodeParams(ctypes.Structure):
     _fields_ = [("q", _vp), ("q_stride_b", _i64), ("q_stride_h", _i64),
-                ("k_cache", _vp), ("v_cache", _vp),
+                ("k_cache", _vp), ("v_cache", _vp), ("num_pages", _i64),
                 ("kv_stride_page", _i64), ("kv_stride_token", _i64), ("kv_stride_head", _i64),
                 ("kv_layout", ctypes.c_int), ("qk_layout", ctypes.c_int),
                 ("indptr", _vp), ("indices", _vp), ("last_page_len", _vp),

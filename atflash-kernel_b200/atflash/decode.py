@@ -187,6 +187,7 @@ class BatchDecodeWithPagedKVCacheWrapper:
         a = _ffi.AtfDecodeParams()
         a.q, a.q_stride_b, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
         a.k_cache, a.v_cache = kc.data_ptr(), vc.data_ptr()
+        a.num_pages = kc.shape[0]
         a.kv_stride_page, a.kv_stride_token, a.kv_stride_head = s_page, s_tok, s_head
         a.kv_layout = _ffi.ATF_KV_NHD if self._kv_layout == "NHD" else _ffi.ATF_KV_HND
         a.qk_layout = P["layout"]

@@ -65,7 +65,7 @@ __device__ __forceinline__ bool aborted(const AbortCtl& a) {
   return false;
 }
 
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const AbortCtl& a,
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const AbortCtl& a,
                                             int code) {
   uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {

@@ -26,6 +26,7 @@
 #include <math.h>
 
 #include "atf_internal.h"
+#include "atf_ptx.cuh"
 
 namespace atf {
 namespace decode {
@@ -364,6 +365,337 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 
 }  // namespace decode
 
+namespace decode_tma {
+
+// Warp-specialised variant for page sizes 16..256 that divide 64 or are
+// multiples of it: one producer warp moves whole page slices with TMA (K one
+// 16-dim level at a time, only up to the slice's window depth; V as two
+// 64-dim halves), four consumer warps run the same mma.sync math as the
+// cp.async kernel above on 16-key groups.
+constexpr int STAGE_KEYS = 64;
+constexpr int NSTAGE = 3;
+constexpr int CONSUMERS = 4;
+constexpr int THREADS = (CONSUMERS + 1) * 32;
+constexpr uint32_t KLEVEL_BYTES = STAGE_KEYS * 32;  // 64 rows x 16 dims
+constexpr uint32_t K_BYTES = 8 * KLEVEL_BYTES;
+constexpr uint32_t VHALF_BYTES = STAGE_KEYS * 128;  // 64 rows x 64 dims
+constexpr uint32_t STAGE_BYTES = K_BYTES + 2 * VHALF_BYTES;
+constexpr int MAX_ITEM_KEYS = 16384;  // atf_decode_plan never makes longer items
+constexpr int MAX_ITEM_PAGES = MAX_ITEM_KEYS / 16 + 1;
+constexpr uint32_t OFF_BAR = NSTAGE * STAGE_BYTES;
+constexpr uint32_t OFF_PAGES = OFF_BAR + 64;
+constexpr uint32_t SMEM_BYTES = OFF_PAGES + 4 * MAX_ITEM_PAGES + 1024;
+constexpr uint32_t FULLMASK = 0xffffffffu;
+
+struct Args {
+  decode::Args d;
+  int rows;         // rows per TMA box: min(page_size, 64)
+  int heads_inner;  // 1: tensor-map dims (d, head, token, page); 0: (d, token, head, page)
+  int* err;
+};
+
+__device__ __forceinline__ int snap_levels(const decode::Args& a, long long z) {
+  if (a.window == ATF_WINDOW_OFF) return 8;
+  int L = 0;
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi16[i]) >= z) ? 1 : 0;
+  return L < 1 ? 1 : L;
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+    decode_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const decode::Args& a = args.d;
+  const uint32_t raw = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  const uint32_t sb = (raw + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw);
+  auto full_bar = [&](int s) { return sb + OFF_BAR + 8u * s; };
+  auto empty_bar = [&](int s) { return sb + OFF_BAR + 8u * (NSTAGE + s); };
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sp + OFF_BAR + 8 * 2 * NSTAGE);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.x, hk = blockIdx.y;
+  const int b = a.items[4 * item + 0];
+  const int k_beg = a.items[4 * item + 1];
+  const int k_end = a.items[4 * item + 2];
+  const int pg0 = a.indptr[b];
+  const int npages = a.indptr[b + 1] - pg0;
+  const long long kv_len =
+      npages > 0 ? static_cast<long long>(npages - 1) * a.page_size + a.last_page_len[b] : 0;
+  const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
+  const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+  const int G = a.G;
+  const int hq0 = hk * G;
+  const int nst = (k_end - k_beg + STAGE_KEYS - 1) / STAGE_KEYS;
+
+  if (tid == 0) {
+    *s_abort = (args.err != nullptr && *reinterpret_cast<volatile int*>(args.err) != 0) ? 1 : 0;
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), CONSUMERS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const AbortCtl ab{s_abort, args.err};
+  const bool start_ok = (*s_abort == 0);
+
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  const int g = lane >> 2, t4 = lane & 3;
+
+  if (start_ok && warp == CONSUMERS) {
+    // ------------------------------------------------------------ producer
+    const int R = args.rows;
+    // the item's page list, staged once so that no TMA waits on a global load
+    int* s_pages = reinterpret_cast<int*>(sp + OFF_PAGES);
+    const int first_page = k_beg / a.page_size;
+    const int n_item_pages = (k_end - 1) / a.page_size - first_page + 1;
+    for (int i = lane; i < n_item_pages; i += 32) s_pages[i] = a.indices[pg0 + first_page + i];
+    __syncwarp();
+    int issued = 0;
+    for (int s = 0; s < nst; ++s) {
+      const int buf = s % NSTAGE;
+      if (!__all_sync(FULLMASK, mbar_wait(empty_bar(buf), ((s / NSTAGE) & 1) ^ 1, ab, kDevErrTimeout)))
+        break;
+      const int k0 = k_beg + s * STAGE_KEYS;
+      const int nkeys = min(STAGE_KEYS, k_end - k0);
+      // Lane-parallel issue: lane = (slice lane/8, level lane%8). Each lane
+      // issues its own K-level box (if the level is in the slice's window) and
+      // lanes 0/1 of a slice also issue the two V halves, so one stage costs two
+      // TMA instructions instead of a serial loop over up to 40 boxes.
+      const int slice = lane >> 3, lvl = lane & 7;
+      const int r0 = slice * R;
+      const bool live = r0 < nkeys && slice * R < STAGE_KEYS;
+      int L = 0;
+      if (live) {
+        const int n_last = min(k0 + r0 + R, k_end) - 1;
+        L = snap_levels(a, q_pos - (pos0 + n_last));
+      }
+      // bytes: sum over slices (lanes 8*slice carry them)
+      uint32_t my_bytes = (live && lvl == 0) ? static_cast<uint32_t>(R) * (32u * L + 256u) : 0u;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) my_bytes += __shfl_xor_sync(FULLMASK, my_bytes, off);
+      mbar_arrive_expect_tx_elect(full_bar(buf), my_bytes);
+      __syncwarp();
+      const uint32_t kdst = sb + buf * STAGE_BYTES;
+      const uint32_t vdst = kdst + K_BYTES;
+      if (live && (lvl < L || lvl < 2)) {
+        const int n = k0 + r0;
+        const int page = s_pages[n / a.page_size - first_page];
+        const int tok = n % a.page_size;
+        const int c1 = args.heads_inner ? hk : tok;
+        const int c2 = args.heads_inner ? tok : hk;
+        if (lvl < L) tma_load_4d(kdst + lvl * KLEVEL_BYTES + r0 * 32, &tmK, full_bar(buf), 16 * lvl, c1, c2, page);
+        if (lvl < 2) tma_load_4d(vdst + lvl * VHALF_BYTES + r0 * 128, &tmV, full_bar(buf), 64 * lvl, c1, c2, page);
+      }
+      __syncwarp();
+      issued = s + 1;
+    }
+    for (int s = issued - NSTAGE; s < issued; ++s)
+      if (s >= 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(full_bar(s % NSTAGE), (s / NSTAGE) & 1))
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+  } else if (start_ok) {
+    // ------------------------------------------------------------ consumers
+    uint32_t qa[8][4];
+    {
+      const __nv_bfloat16* qrow0 =
+          a.q + static_cast<long long>(b) * a.q_sb + static_cast<long long>(hq0 + g) * a.q_sh;
+      const __nv_bfloat16* qrow1 = qrow0 + 8 * a.q_sh;
+      const bool v0 = g < G, v1 = g + 8 < G;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c0 = 16 * i + 2 * t4, c1 = 16 * i + 8 + 2 * t4;
+        qa[i][0] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0) : 0u;
+        qa[i][1] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0) : 0u;
+        qa[i][2] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c1) : 0u;
+        qa[i][3] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c1) : 0u;
+      }
+    }
+    const int mi = lane >> 3;
+    for (int s = 0; s < nst; ++s) {
+      const int buf = s % NSTAGE;
+      if (!__all_sync(FULLMASK, mbar_wait(full_bar(buf), (s / NSTAGE) & 1, ab, kDevErrTimeout))) break;
+      const uint32_t kb = sb + buf * STAGE_BYTES;
+      const uint32_t vb = kb + K_BYTES;
+      const int key0 = k_beg + s * STAGE_KEYS + warp * 16;
+      if (key0 < k_end) {
+        const int last = min(key0 + 15, k_end - 1);
+        const int Lmax = snap_levels(a, q_pos - (pos0 + last));
+        const int Lmin = snap_levels(a, q_pos - (pos0 + key0));
+        // rows past the item end may hold anything (the TMA box covers the
+        // whole page slice): zero their V so that P = 0 rows add exactly 0
+        if (last < key0 + 15) {
+          const int bad0 = last - key0 + 1;  // first invalid row in this group
+          for (int e = lane; e < (16 - bad0) * 16; e += 32) {
+            const int row = warp * 16 + bad0 + e / 16, cc = e % 16;
+            *reinterpret_cast<uint4*>(sp + (vb - sb) + (cc >> 3) * VHALF_BYTES + row * 128 +
+                                      16 * ((cc & 7) ^ (row & 7))) = make_uint4(0, 0, 0, 0);
+          }
+          // order these generic-proxy writes before any later TMA write here
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+        }
+        float sc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
+        const uint32_t krow = static_cast<uint32_t>(lrow * 32 + 16 * ((mi & 1) ^ ((lrow >> 2) & 1)));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i < Lmax) {
+            uint32_t b0, b1, b2, b3;
+            decode::ldsm_x4(kb + i * KLEVEL_BYTES + krow, b0, b1, b2, b3);
+            if (i < Lmin) {
+              decode::mma16816(sc[0], qa[i], b0, b1);
+              decode::mma16816(sc[1], qa[i], b2, b3);
+            } else {
+              // level i is active only for the newer keys of the group
+              float tmp[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+              decode::mma16816(tmp[0], qa[i], b0, b1);
+              decode::mma16816(tmp[1], qa[i], b2, b3);
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
+                  if (key <= last && i < snap_levels(a, q_pos - (pos0 + key))) sc[nt][e] += tmp[nt][e];
+                }
+            }
+          }
+        }
+        float mloc[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
+            const float v = key <= last ? sc[nt][e] * a.scale_log2 : -INFINITY;
+            sc[nt][e] = v;
+            mloc[e >> 1] = fmaxf(mloc[e >> 1], v);
+          }
+        float alpha[2], psum[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 1));
+          mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 2));
+          const float mnew = fmaxf(m_run[r], mloc[r]);
+          alpha[r] = (m_run[r] == -INFINITY) ? 0.f : decode::ex2f(m_run[r] - mnew);
+          m_run[r] = mnew;
+          psum[r] = 0.f;
+        }
+        uint32_t pfrag[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float p0 = decode::ex2f(sc[nt][0] - m_run[0]);
+          const float p1 = decode::ex2f(sc[nt][1] - m_run[0]);
+          const float p2 = decode::ex2f(sc[nt][2] - m_run[1]);
+          const float p3 = decode::ex2f(sc[nt][3] - m_run[1]);
+          psum[0] += p0 + p1;
+          psum[1] += p2 + p3;
+          pfrag[2 * nt + 0] = decode::pack2(p0, p1);
+          pfrag[2 * nt + 1] = decode::pack2(p2, p3);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 1);
+          psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 2);
+          l_run[r] = l_run[r] * alpha[r] + psum[r];
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          o[j][0] *= alpha[0];
+          o[j][1] *= alpha[0];
+          o[j][2] *= alpha[1];
+          o[j][3] *= alpha[1];
+        }
+        const int vrow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int dc = 2 * jj + (mi >> 1);  // 8-dim chunk 0..15
+          uint32_t b0, b1, b2, b3;
+          decode::ldsm_x4_t(vb + (dc >> 3) * VHALF_BYTES + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
+                            b0, b1, b2, b3);
+          decode::mma16816(o[2 * jj], pfrag, b0, b1);
+          decode::mma16816(o[2 * jj + 1], pfrag, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(buf));
+    }
+  }
+  __syncthreads();
+
+  // merge the consumer warps' states (stage buffers are free now)
+  float* sm_o = reinterpret_cast<float*>(sp);       // [4][16][128]
+  float* sm_m = sm_o + CONSUMERS * 16 * 128;        // [4][16]
+  float* sm_l = sm_m + CONSUMERS * 16;
+  if (warp < CONSUMERS) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = 8 * j + 2 * t4;
+      sm_o[(warp * 16 + g) * 128 + col] = o[j][0];
+      sm_o[(warp * 16 + g) * 128 + col + 1] = o[j][1];
+      sm_o[(warp * 16 + g + 8) * 128 + col] = o[j][2];
+      sm_o[(warp * 16 + g + 8) * 128 + col + 1] = o[j][3];
+    }
+    if (t4 == 0) {
+      sm_m[warp * 16 + g] = m_run[0];
+      sm_m[warp * 16 + g + 8] = m_run[1];
+      sm_l[warp * 16 + g] = l_run[0];
+      sm_l[warp * 16 + g + 8] = l_run[1];
+    }
+  }
+  __syncthreads();
+  if (!start_ok || *s_abort) return;
+  if (tid < 128) {
+    const int row = tid >> 3, slab = tid & 7;
+    if (row < G) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, sm_m[w * 16 + row]);
+      float wsc[CONSUMERS], L = 0.f;
+#pragma unroll
+      for (int w = 0; w < CONSUMERS; ++w) {
+        const float mw = sm_m[w * 16 + row];
+        wsc[w] = (mw == -INFINITY) ? 0.f : decode::ex2f(mw - M);
+        L += wsc[w] * sm_l[w * 16 + row];
+      }
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      float* dst = a.part_o + (static_cast<long long>(item) * a.Hq + hq0 + row) * 128 + slab * 16;
+#pragma unroll
+      for (int e = 0; e < 16; e += 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) {
+          const float* src = sm_o + (w * 16 + row) * 128 + slab * 16 + e;
+          acc.x += wsc[w] * src[0];
+          acc.y += wsc[w] * src[1];
+          acc.z += wsc[w] * src[2];
+          acc.w += wsc[w] * src[3];
+        }
+        acc.x *= inv;
+        acc.y *= inv;
+        acc.z *= inv;
+        acc.w *= inv;
+        *reinterpret_cast<float4*>(dst + e) = acc;
+      }
+      if (slab == 0)
+        a.part_lse[static_cast<long long>(item) * a.Hq + hq0 + row] =
+            L > 0.f ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+}  // namespace decode_tma
+
 namespace merge {
 
 struct Args {
@@ -471,13 +803,16 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  // Aim for ~8 CTAs per SM in total (2 resident per SM -> ~4 waves), in
-  // 64-key multiples, never below min_chunk keys.
-  const long long target_ctas = 8ll * sms;
+  // Aim for ~16 CTAs per SM in total (2 resident per SM -> ~8 waves, so the
+  // last wave's tail is small), in 64-key multiples, never below min_chunk
+  // keys and never above 16384 keys (the page list of an item is staged in
+  // shared memory by the TMA kernel).
+  const long long target_ctas = 16ll * sms;
   const long long min_chunk = p->min_chunk_keys > 0 ? p->min_chunk_keys : 256;
   long long chunk = (total * p->num_kv_heads + target_ctas - 1) / target_ctas;
   if (chunk < min_chunk) chunk = min_chunk;
   if (p->max_chunk_keys > 0 && chunk > p->max_chunk_keys) chunk = p->max_chunk_keys;
+  if (chunk > decode_tma::MAX_ITEM_KEYS) chunk = decode_tma::MAX_ITEM_KEYS;
   chunk = (chunk + 63) / 64 * 64;
   if (chunk < 64) chunk = 64;
   int n = 0;
@@ -528,6 +863,10 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int ps = p->page_size;
+  const bool tma_path = (ps == 16 || ps == 32 || ps == 64 || ps == 128 || ps == 256) &&
+                        p->qk_layout == ATF_LAYOUT_SORTED_PAIR && p->window != ATF_WINDOW_VEC8 &&
+                        p->num_pages >= 1;
   if (p->num_items > 0) {
     decode::Args a;
     a.q = static_cast<const __nv_bfloat16*>(p->q);
@@ -555,11 +894,41 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
     for (int i = 0; i < ATF_MAX_SLICES; ++i) a.zhi8[i] = p->zhi8[i];
     a.part_o = p->partial_o;
     a.part_lse = p->partial_lse;
-    if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             decode::SMEM_BYTES) != cudaSuccess)
-      return ATF_ERR_CUDA;
     dim3 grid(static_cast<unsigned>(p->num_items), static_cast<unsigned>(p->num_kv_heads));
-    decode::decode_kernel<<<grid, decode::THREADS, decode::SMEM_BYTES, st>>>(a);
+    if (tma_path) {
+      // Tensor maps over the paged cache, dims ordered by stride:
+      // (d, head, token, page) for NHD or (d, token, head, page) for HND.
+      const bool heads_inner = p->kv_stride_head < p->kv_stride_token;
+      const uint64_t d1 = heads_inner ? p->num_kv_heads : ps, d2 = heads_inner ? ps : p->num_kv_heads;
+      const int64_t s1 = heads_inner ? p->kv_stride_head : p->kv_stride_token;
+      const int64_t s2 = heads_inner ? p->kv_stride_token : p->kv_stride_head;
+      const uint64_t dims[4] = {128, d1, d2, static_cast<uint64_t>(p->num_pages)};
+      const uint64_t str[3] = {static_cast<uint64_t>((d1 == 1 ? 8 : s1) * 2),
+                               static_cast<uint64_t>((d2 == 1 ? 8 : s2) * 2),
+                               static_cast<uint64_t>(p->kv_stride_page * 2)};
+      const uint32_t rows = static_cast<uint32_t>(ps < 64 ? ps : 64);
+      const uint32_t kbox[4] = {16, heads_inner ? 1u : rows, heads_inner ? rows : 1u, 1};
+      const uint32_t vbox[4] = {64, heads_inner ? 1u : rows, heads_inner ? rows : 1u, 1};
+      CUtensorMap tk, tv;
+      if ((rc = encode_tiled_bf16(&tk, p->k_cache, 4, dims, str, kbox, CU_TENSOR_MAP_SWIZZLE_32B)) != ATF_OK)
+        return rc;
+      if ((rc = encode_tiled_bf16(&tv, p->v_cache, 4, dims, str, vbox, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
+        return rc;
+      decode_tma::Args ta;
+      ta.d = a;
+      ta.rows = static_cast<int>(rows);
+      ta.heads_inner = heads_inner ? 1 : 0;
+      ta.err = p->error_flag;
+      if (cudaFuncSetAttribute(decode_tma::decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               decode_tma::SMEM_BYTES) != cudaSuccess)
+        return ATF_ERR_CUDA;
+      decode_tma::decode_tma_kernel<<<grid, decode_tma::THREADS, decode_tma::SMEM_BYTES, st>>>(tk, tv, ta);
+    } else {
+      if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               decode::SMEM_BYTES) != cudaSuccess)
+        return ATF_ERR_CUDA;
+      decode::decode_kernel<<<grid, decode::THREADS, decode::SMEM_BYTES, st>>>(a);
+    }
     if (cudaGetLastError() != cudaSuccess) return ATF_ERR_CUDA;
   }
   merge::Args m;

@@ -147,6 +147,7 @@ typedef struct {
   int64_t q_stride_b, q_stride_h;
   const void* k_cache; /* bf16 pages: NHD [P, page, Hkv, 128] or HND [P, Hkv, page, 128] */
   const void* v_cache;
+  int64_t num_pages;    /* pages in the cache (page indices must be < num_pages) */
   int64_t kv_stride_page, kv_stride_token, kv_stride_head; /* same for k and v */
   int kv_layout;        /* ATF_KV_* (informational; strides carry the layout) */
   int qk_layout;        /* pair order of q and the cached k */
