@@ -17,9 +17,10 @@ ATF_LAYOUT_SORTED_PAIR, ATF_LAYOUT_ROTATE_HALF = 0, 1
 ATF_KV_NHD, ATF_KV_HND = 0, 1
 ATF_WINDOW_OFF, ATF_WINDOW_SNAP16, ATF_WINDOW_VEC8 = 0, 1, 2
 ATF_DTYPE_BF16, ATF_DTYPE_F32 = 0, 1
+ATF_NOALLOC_MAX_PARTIAL_ROWS = 16384
 
 EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_window_deff",
-            "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_lse_merge",
+            "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
             "atf_rope_pack", "atf_status_string", "atf_version", "atf_read_error_flag")
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -112,6 +113,7 @@ def load() -> ctypes.CDLL:
             lib.atf_prefill_fwd.argtypes = [P(AtfPrefillParams), _vp]
             lib.atf_decode_plan.argtypes = [P(AtfDecodePlanParams), P(_i32), _i32, P(_i32), P(AtfDecodePlan)]
             lib.atf_decode_run.argtypes = [P(AtfDecodeParams), _vp]
+            lib.atf_decode_run_noalloc.argtypes = [P(AtfDecodeParams), _vp]
             lib.atf_lse_merge.argtypes = [P(AtfMergeParams), _vp]
             lib.atf_rope_pack.argtypes = [P(AtfRopeParams), _vp]
             lib.atf_status_string.argtypes = [ctypes.c_int]

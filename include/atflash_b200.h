@@ -176,6 +176,36 @@ typedef struct {
 /* Paged-KV GQA split-KV decode followed by the LSE merge of its splits. */
 int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream);
 
+/* atf_decode_run without any allocation. It has no counterpart in the
+ * reference, whose decode always takes a workspace that the caller allocated.
+ *
+ * Who needs it: callers that cannot call cudaMalloc. Examples are a serving
+ * engine that gave all free device memory to its KV-cache pool up front, and a
+ * host whose step loop must not allocate because cudaMalloc and cudaFree
+ * synchronise the device. Here the split workspace (partial_o, partial_lse)
+ * comes from one fixed scratch array compiled into this library, one per
+ * device. The function itself calls no cudaMalloc, cudaFree or allocating
+ * library routine.
+ *
+ * Rules:
+ *  - p->partial_o and p->partial_lse must be NULL. Every other field means what
+ *    it means for atf_decode_run.
+ *  - Limit: num_items * num_qo_heads <= ATF_NOALLOC_MAX_PARTIAL_ROWS. Larger
+ *    plans return ATF_ERR_WORKSPACE and launch nothing; plan them with a larger
+ *    min_chunk_keys, or use atf_decode_run.
+ *  - Nothing in the scratch has to start at zero: each call writes every row it
+ *    reads. The caller's error_flag, when given, must be zero on entry, as for
+ *    atf_decode_run.
+ *  - All calls on one device share the scratch. Calls that overlap on the GPU
+ *    (on different streams with no ordering between them, or from several
+ *    threads) race and corrupt each other's output. Issue them on one stream,
+ *    or order them with events.
+ *  - The first call on each device looks up the scratch address with
+ *    cudaGetSymbolAddress. Make that first call before any stream capture
+ *    begins on that device. */
+#define ATF_NOALLOC_MAX_PARTIAL_ROWS 16384 /* 8 MiB + 64 KiB of fp32 scratch per device */
+int atf_decode_run_noalloc(const AtfDecodeParams* p, atf_stream_t stream);
+
 /* ------------------------------------------------------------------ merge */
 
 typedef struct {
