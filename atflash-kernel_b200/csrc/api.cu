@@ -19,7 +19,7 @@ std::once_flag g_encode_once;
 
 int encode_tiled_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                       const uint64_t* strides_bytes, const uint32_t* box,
-                      CUtensorMapSwizzle swizzle) {
+                      CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promotion) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -42,7 +42,7 @@ int encode_tiled_bf16(CUtensorMap* map, const void* base, int rank, const uint64
   }
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
                         const_cast<void*>(base), d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle, promotion,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ATF_OK : ATF_ERR_CUDA;
 }

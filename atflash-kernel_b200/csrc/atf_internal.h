@@ -16,7 +16,8 @@ constexpr int kDevErrTimeout = 1;
 // dims / strides are innermost first; strides are in bytes for dims 1..rank-1.
 int encode_tiled_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                       const uint64_t* strides_bytes, const uint32_t* box,
-                      CUtensorMapSwizzle swizzle);
+                      CUtensorMapSwizzle swizzle,
+                      CUtensorMapL2promotion promotion = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
 // True when the current device is an sm_100 part.
 int check_device(int* device_out);

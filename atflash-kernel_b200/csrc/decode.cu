@@ -368,18 +368,24 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
 namespace decode_tma {
 
 // Warp-specialised variant for page sizes 16..256 that divide 64 or are
-// multiples of it: one producer warp moves whole page slices with TMA (K one
-// 16-dim level at a time, only up to the slice's window depth; V as two
-// 64-dim halves), four consumer warps run the same mma.sync math as the
-// cp.async kernel above on 16-key groups.
+// multiples of it. A stage is 64 keys = 64/R page slices of R = min(page, 64)
+// rows. One producer warp moves each slice with two 5-d TMA boxes: K as
+// [L levels][R rows][16 dims] with L the slice's window depth (one tensor map
+// per L, so the out-of-window levels are never requested), V as
+// [2 halves][R rows][64 dims]. Four consumer warps run the same mma.sync math
+// as the cp.async kernel above on 16-key groups; a group never straddles two
+// slices (R >= 16).
+//
+// Shared memory of one stage: K slices at s * 256R (level l of the slice at
+// + l * 32R, SW32), then V slices at 16 KB + s * 256R (half h at + h * 128R,
+// SW128). For R = 64 this is the plain level-major / half-major layout.
 constexpr int STAGE_KEYS = 64;
 constexpr int NSTAGE = 3;
 constexpr int CONSUMERS = 4;
 constexpr int THREADS = (CONSUMERS + 1) * 32;
-constexpr uint32_t KLEVEL_BYTES = STAGE_KEYS * 32;  // 64 rows x 16 dims
-constexpr uint32_t K_BYTES = 8 * KLEVEL_BYTES;
-constexpr uint32_t VHALF_BYTES = STAGE_KEYS * 128;  // 64 rows x 64 dims
-constexpr uint32_t STAGE_BYTES = K_BYTES + 2 * VHALF_BYTES;
+constexpr uint32_t K_BYTES = STAGE_KEYS * 256;  // 64 rows x 8 levels x 16 dims
+constexpr uint32_t V_BYTES = STAGE_KEYS * 256;  // 64 rows x 128 dims
+constexpr uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
 constexpr int MAX_ITEM_KEYS = 16384;  // atf_decode_plan never makes longer items
 constexpr int MAX_ITEM_PAGES = MAX_ITEM_KEYS / 16 + 1;
 constexpr uint32_t OFF_BAR = NSTAGE * STAGE_BYTES;
@@ -389,9 +395,14 @@ constexpr uint32_t FULLMASK = 0xffffffffu;
 
 struct Args {
   decode::Args d;
-  int rows;         // rows per TMA box: min(page_size, 64)
-  int heads_inner;  // 1: tensor-map dims (d, head, token, page); 0: (d, token, head, page)
+  int rows;  // rows per TMA box: min(page_size, 64)
   int* err;
+};
+
+// K tensor maps over (16 dims, token, level, kv head, page); map L-1 has the
+// box {16, rows, L, 1, 1}.
+struct KMaps {
+  CUtensorMap lv[ATF_MAX_LEVELS];
 };
 
 __device__ __forceinline__ int snap_levels(const decode::Args& a, long long z) {
@@ -403,7 +414,7 @@ __device__ __forceinline__ int snap_levels(const decode::Args& a, long long z) {
 }
 
 __global__ void __launch_bounds__(THREADS, 2)
-    decode_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    decode_tma_kernel(const __grid_constant__ KMaps tmK, const __grid_constant__ CUtensorMap tmV,
                       const Args args) {
   extern __shared__ uint8_t smem_raw[];
   const decode::Args& a = args.d;
@@ -451,6 +462,8 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (start_ok && warp == CONSUMERS) {
     // ------------------------------------------------------------ producer
     const int R = args.rows;
+    if (lane < ATF_MAX_LEVELS) tma_prefetch_desc(&tmK.lv[lane]);
+    if (lane == ATF_MAX_LEVELS) tma_prefetch_desc(&tmV);
     // the item's page list, staged once so that no TMA waits on a global load
     int* s_pages = reinterpret_cast<int*>(sp + OFF_PAGES);
     const int first_page = k_beg / a.page_size;
@@ -464,34 +477,31 @@ __global__ void __launch_bounds__(THREADS, 2)
         break;
       const int k0 = k_beg + s * STAGE_KEYS;
       const int nkeys = min(STAGE_KEYS, k_end - k0);
-      // Lane-parallel issue: lane = (slice lane/8, level lane%8). Each lane
-      // issues its own K-level box (if the level is in the slice's window) and
-      // lanes 0/1 of a slice also issue the two V halves, so one stage costs two
-      // TMA instructions instead of a serial loop over up to 40 boxes.
-      const int slice = lane >> 3, lvl = lane & 7;
+      // Lane-parallel issue: lane 2s moves slice s of K (its window depth L
+      // picks the tensor map), lane 2s+1 moves slice s of V.
+      const int slice = lane >> 1, is_v = lane & 1;
       const int r0 = slice * R;
-      const bool live = r0 < nkeys && slice * R < STAGE_KEYS;
+      const bool live = r0 < nkeys && r0 < STAGE_KEYS;
       int L = 0;
       if (live) {
         const int n_last = min(k0 + r0 + R, k_end) - 1;
         L = snap_levels(a, q_pos - (pos0 + n_last));
       }
-      // bytes: sum over slices (lanes 8*slice carry them)
-      uint32_t my_bytes = (live && lvl == 0) ? static_cast<uint32_t>(R) * (32u * L + 256u) : 0u;
+      // bytes: sum over slices (the K lanes carry them)
+      uint32_t my_bytes = (live && !is_v) ? static_cast<uint32_t>(R) * (32u * L + 256u) : 0u;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) my_bytes += __shfl_xor_sync(FULLMASK, my_bytes, off);
       mbar_arrive_expect_tx_elect(full_bar(buf), my_bytes);
       __syncwarp();
-      const uint32_t kdst = sb + buf * STAGE_BYTES;
-      const uint32_t vdst = kdst + K_BYTES;
-      if (live && (lvl < L || lvl < 2)) {
+      if (live) {
         const int n = k0 + r0;
         const int page = s_pages[n / a.page_size - first_page];
         const int tok = n % a.page_size;
-        const int c1 = args.heads_inner ? hk : tok;
-        const int c2 = args.heads_inner ? tok : hk;
-        if (lvl < L) tma_load_4d(kdst + lvl * KLEVEL_BYTES + r0 * 32, &tmK, full_bar(buf), 16 * lvl, c1, c2, page);
-        if (lvl < 2) tma_load_4d(vdst + lvl * VHALF_BYTES + r0 * 128, &tmV, full_bar(buf), 64 * lvl, c1, c2, page);
+        const uint32_t dst = sb + buf * STAGE_BYTES + (is_v ? K_BYTES : 0u) + static_cast<uint32_t>(r0) * 256u;
+        if (is_v)
+          tma_load_5d(dst, &tmV, full_bar(buf), 0, tok, 0, hk, page);
+        else
+          tma_load_5d(dst, &tmK.lv[L - 1], full_bar(buf), 0, tok, 0, hk, page);
       }
       __syncwarp();
       issued = s + 1;
@@ -520,6 +530,12 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
     }
     const int mi = lane >> 3;
+    // this warp's 16-key group lies in slice sw = 16 warp / R; the offsets below
+    // turn a stage-relative row (lrow / vrow) into that slice's layout
+    const uint32_t R = static_cast<uint32_t>(args.rows);
+    const uint32_t sw = static_cast<uint32_t>(warp * 16) / R;
+    const uint32_t k_slice = sw * R * 224u, v_slice = sw * R * 128u;
+    const uint32_t lstride = 32u * R, hstride = 128u * R;
     for (int s = 0; s < nst; ++s) {
       const int buf = s % NSTAGE;
       if (!__all_sync(FULLMASK, mbar_wait(full_bar(buf), (s / NSTAGE) & 1, ab, kDevErrTimeout))) break;
@@ -536,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           const int bad0 = last - key0 + 1;  // first invalid row in this group
           for (int e = lane; e < (16 - bad0) * 16; e += 32) {
             const int row = warp * 16 + bad0 + e / 16, cc = e % 16;
-            *reinterpret_cast<uint4*>(sp + (vb - sb) + (cc >> 3) * VHALF_BYTES + row * 128 +
+            *reinterpret_cast<uint4*>(sp + (vb - sb) + v_slice + (cc >> 3) * hstride + row * 128 +
                                       16 * ((cc & 7) ^ (row & 7))) = make_uint4(0, 0, 0, 0);
           }
           // order these generic-proxy writes before any later TMA write here
@@ -552,7 +568,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         for (int i = 0; i < 8; ++i) {
           if (i < Lmax) {
             uint32_t b0, b1, b2, b3;
-            decode::ldsm_x4(kb + i * KLEVEL_BYTES + krow, b0, b1, b2, b3);
+            decode::ldsm_x4(kb + k_slice + i * lstride + krow, b0, b1, b2, b3);
             if (i < Lmin) {
               decode::mma16816(sc[0], qa[i], b0, b1);
               decode::mma16816(sc[1], qa[i], b2, b3);
@@ -621,7 +637,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         for (int jj = 0; jj < 8; ++jj) {
           const int dc = 2 * jj + (mi >> 1);  // 8-dim chunk 0..15
           uint32_t b0, b1, b2, b3;
-          decode::ldsm_x4_t(vb + (dc >> 3) * VHALF_BYTES + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
+          decode::ldsm_x4_t(vb + v_slice + (dc >> 3) * hstride + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
                             b0, b1, b2, b3);
           decode::mma16816(o[2 * jj], pfrag, b0, b1);
           decode::mma16816(o[2 * jj + 1], pfrag, b2, b3);
@@ -896,28 +912,36 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
     a.part_lse = p->partial_lse;
     dim3 grid(static_cast<unsigned>(p->num_items), static_cast<unsigned>(p->num_kv_heads));
     if (tma_path) {
-      // Tensor maps over the paged cache, dims ordered by stride:
-      // (d, head, token, page) for NHD or (d, token, head, page) for HND.
-      const bool heads_inner = p->kv_stride_head < p->kv_stride_token;
-      const uint64_t d1 = heads_inner ? p->num_kv_heads : ps, d2 = heads_inner ? ps : p->num_kv_heads;
-      const int64_t s1 = heads_inner ? p->kv_stride_head : p->kv_stride_token;
-      const int64_t s2 = heads_inner ? p->kv_stride_token : p->kv_stride_head;
-      const uint64_t dims[4] = {128, d1, d2, static_cast<uint64_t>(p->num_pages)};
-      const uint64_t str[3] = {static_cast<uint64_t>((d1 == 1 ? 8 : s1) * 2),
-                               static_cast<uint64_t>((d2 == 1 ? 8 : s2) * 2),
-                               static_cast<uint64_t>(p->kv_stride_page * 2)};
+      // 5-d tensor maps over the paged cache: (dims of a level or half, token,
+      // level or half, kv head, page). The level/half axis is a view of
+      // head_dim, so one box moves a whole page slice. A size-1 axis gets a
+      // placeholder stride (its stride is never used and may be anything).
+      auto stride_b = [](uint64_t size, int64_t stride_elems) {
+        return size == 1 ? 256ull : static_cast<uint64_t>(stride_elems) * 2ull;
+      };
+      const uint64_t hkv = static_cast<uint64_t>(p->num_kv_heads), npg = static_cast<uint64_t>(p->num_pages);
+      const uint64_t kdims[5] = {16, static_cast<uint64_t>(ps), ATF_MAX_LEVELS, hkv, npg};
+      const uint64_t vdims[5] = {64, static_cast<uint64_t>(ps), 2, hkv, npg};
+      const uint64_t kstr[4] = {stride_b(ps, p->kv_stride_token), 32, stride_b(hkv, p->kv_stride_head),
+                                stride_b(npg, p->kv_stride_page)};
+      const uint64_t vstr[4] = {kstr[0], 128, kstr[2], kstr[3]};
       const uint32_t rows = static_cast<uint32_t>(ps < 64 ? ps : 64);
-      const uint32_t kbox[4] = {16, heads_inner ? 1u : rows, heads_inner ? rows : 1u, 1};
-      const uint32_t vbox[4] = {64, heads_inner ? 1u : rows, heads_inner ? rows : 1u, 1};
-      CUtensorMap tk, tv;
-      if ((rc = encode_tiled_bf16(&tk, p->k_cache, 4, dims, str, kbox, CU_TENSOR_MAP_SWIZZLE_32B)) != ATF_OK)
-        return rc;
-      if ((rc = encode_tiled_bf16(&tv, p->v_cache, 4, dims, str, vbox, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
+      decode_tma::KMaps tk;
+      CUtensorMap tv;
+      // K: no L2 promotion, so that a slice's out-of-window levels (the tail
+      // of each 256-byte row) are not fetched from HBM along with its prefix
+      for (int L = 1; L <= ATF_MAX_LEVELS; ++L) {
+        const uint32_t kbox[5] = {16, rows, static_cast<uint32_t>(L), 1, 1};
+        if ((rc = encode_tiled_bf16(&tk.lv[L - 1], p->k_cache, 5, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_32B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_NONE)) != ATF_OK)
+          return rc;
+      }
+      const uint32_t vbox[5] = {64, rows, 2, 1, 1};
+      if ((rc = encode_tiled_bf16(&tv, p->v_cache, 5, vdims, vstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
         return rc;
       decode_tma::Args ta;
       ta.d = a;
       ta.rows = static_cast<int>(rows);
-      ta.heads_inner = heads_inner ? 1 : 0;
       ta.err = p->error_flag;
       if (cudaFuncSetAttribute(decode_tma::decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                decode_tma::SMEM_BYTES) != cudaSuccess)
