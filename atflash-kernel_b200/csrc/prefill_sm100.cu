@@ -141,13 +141,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work unit: longest query blocks first; heads of one kv group adjacent.
-  const int nbh = a.B * a.Hq;
-  const int qblk = a.n_qblk - 1 - static_cast<int>(blockIdx.x) / nbh;
-  const int bh = static_cast<int>(blockIdx.x) % nbh;
-  const int bi = bh / a.Hq;
-  const int h = bh % a.Hq;
-  const int hk = h / a.G;
+  // Work unit order: one (batch, kv head) group at a time, longest query
+  // blocks first inside it, the G query heads of the group adjacent. The CTAs
+  // resident together then read a single kv head's K/V, whose causal range
+  // (256 B x 2 per key) stays in L2, so HBM sees each K/V byte about once.
+  const int Hkv = a.Hq / a.G;
+  const int per_group = a.n_qblk * a.G;
+  const int grp = static_cast<int>(blockIdx.x) / per_group;
+  const int rem = static_cast<int>(blockIdx.x) % per_group;
+  const int qblk = a.n_qblk - 1 - rem / a.G;
+  const int bi = grp / Hkv;
+  const int hk = grp % Hkv;
+  const int h = hk * a.G + rem % a.G;
   int row0[NQ], nk[NQ];
 #pragma unroll
   for (int t = 0; t < NQ; ++t) {
