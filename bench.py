@@ -38,8 +38,10 @@ import torch.distributed as dist  # noqa: E402
 
 N_CTX, HQ, HKV, D, THETA, K_RET = 131072, 28, 4, 128, 1e7, 2.0
 METRIC = "Windowed-attn prefill ms @128K/512K + decode µs/step @128K, window on vs off"
-# dram bytes of one prefill launch from ncu (profiles/prefill_sm100_128k.md); None = not captured
-PREFILL_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one 131072-token k=2 prefill
+# launch, from a one-pass ncu capture of the full-size launch (summarised under
+# profiles/ with its command): 2.28 GB read + 0.902 GB written
+PREFILL_TRAFFIC_BYTES = 2.28e9 + 0.902e9
 
 
 def load_peaks():
@@ -166,7 +168,7 @@ def prefill_inputs(device, copies=2, seed=2026):
     return out
 
 
-def cpu_baseline_sample(n_tiles=4, heads=7, k_ret=K_RET):
+def cpu_baseline_sample(n_tiles=20, heads=7, k_ret=K_RET):
     """Time the numpy oracle on `n_tiles` query tiles x `heads` heads (one kv
     group) of the config-2 workload; extrapolate to the full prefill by FLOPs."""
     import numpy as np
