@@ -353,7 +353,7 @@ def main():
                 "frac": achieved / peaks["bf16_tflops"],
                 "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"] + " (burst; kernel timed alone)",
-                "traffic": PREFILL_TRAFFIC_BYTES,
+                "traffic": PREFILL_TRAFFIC_BYTES if world == 1 and N_CTX == 131072 else None,
                 "work": "windowed FLOPs 2*Hq*sum_unmasked(D_eff(tile)+d) per launch set of this rank",
                 "flops_per_step": my_flops}
         line = {"metric": METRIC, "value": ms_on, "unit": "ms", "n_gpus": world, "steps": args.steps,

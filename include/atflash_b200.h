@@ -14,7 +14,8 @@
  *    in elements and the innermost (head_dim) stride is 1.
  *  - Kernels run on the caller's stream. The library keeps no mutable global
  *    state except the lazily loaded driver entry point used to encode TMA
- *    descriptors.
+ *    descriptors and, for atf_decode_run_noalloc only, its scratch array and
+ *    the per-device address of that array.
  *  - head_dim is 128. GQA group sizes 1..16 (1/2/3/4/7/8 are the tested ones).
  *  - Device-side waits are bounded. A wait that expires writes a non-zero code
  *    to params->error_flag (if not NULL) and the kernel returns early; read it
