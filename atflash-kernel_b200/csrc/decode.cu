@@ -726,12 +726,21 @@ struct Args {
   float* lse_out;
 };
 
-// One warp per (request, head); lane covers 4 dims.
-__global__ void merge_kernel(const Args a) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= a.B * a.H) return;
-  const int b = w / a.H, h = w % a.H;
+// One block of MERGE_WARPS warps per (request, head); a lane covers 4 dims.
+// The block first finds the largest part LSE, then each warp accumulates the
+// weighted partial outputs of every MERGE_WARPS-th part (4 loads in flight per
+// lane), and warp 0 adds up the warps' sums. A request split into hundreds of
+// parts (a 1M-token context) thus merges in a few load latencies instead of
+// one per part.
+constexpr int MERGE_WARPS = 8;
+
+__global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
+  __shared__ float s_red[MERGE_WARPS];
+  __shared__ float4 s_acc[MERGE_WARPS][32];
+  __shared__ float s_l[MERGE_WARPS];
+  const int bh = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = bh / a.H, h = bh % a.H;
   int p0, p1;
   long long stride_p;  // distance between consecutive parts of this (b, h), in rows of H
   long long base;
@@ -746,21 +755,66 @@ __global__ void merge_kernel(const Args a) {
     base = static_cast<long long>(b) * a.H + h;
     stride_p = static_cast<long long>(a.B) * a.H;
   }
+  const int n = p1 - p0;
   const float cvt = a.lse_log2 ? 1.0f : 1.4426950408889634f;  // to log2
   float M = -INFINITY;
-  for (int p = p0; p < p1; ++p) M = fmaxf(M, a.pl[base + (p - p0) * stride_p] * cvt);
+  for (int i = threadIdx.x; i < n; i += MERGE_WARPS * 32) M = fmaxf(M, a.pl[base + i * stride_p] * cvt);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+#pragma unroll
+  for (int w = 1; w < MERGE_WARPS; ++w) M = fmaxf(M, s_red[w]);
+
   float L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int p = p0; p < p1; ++p) {
-    const long long r = base + (p - p0) * stride_p;
+  auto add = [&](int i) {
+    const long long r = base + i * stride_p;
     const float lp = a.pl[r] * cvt;
     const float wgt = (lp == -INFINITY) ? 0.f : exp2f(lp - M);
-    L += wgt;
     const float4 v = *reinterpret_cast<const float4*>(a.po + r * 128 + lane * 4);
+    L += wgt;
     acc.x += wgt * v.x;
     acc.y += wgt * v.y;
     acc.z += wgt * v.z;
     acc.w += wgt * v.w;
+  };
+  int i = warp;
+  for (; i + 3 * MERGE_WARPS < n; i += 4 * MERGE_WARPS) {
+    // four independent parts per iteration keep four loads in flight
+    const long long r0 = base + i * stride_p, r1 = r0 + MERGE_WARPS * stride_p;
+    const long long r2 = r1 + MERGE_WARPS * stride_p, r3 = r2 + MERGE_WARPS * stride_p;
+    const float l0 = a.pl[r0] * cvt, l1 = a.pl[r1] * cvt, l2 = a.pl[r2] * cvt, l3 = a.pl[r3] * cvt;
+    const float4 v0 = *reinterpret_cast<const float4*>(a.po + r0 * 128 + lane * 4);
+    const float4 v1 = *reinterpret_cast<const float4*>(a.po + r1 * 128 + lane * 4);
+    const float4 v2 = *reinterpret_cast<const float4*>(a.po + r2 * 128 + lane * 4);
+    const float4 v3 = *reinterpret_cast<const float4*>(a.po + r3 * 128 + lane * 4);
+    const float w0 = (l0 == -INFINITY) ? 0.f : exp2f(l0 - M);
+    const float w1 = (l1 == -INFINITY) ? 0.f : exp2f(l1 - M);
+    const float w2 = (l2 == -INFINITY) ? 0.f : exp2f(l2 - M);
+    const float w3 = (l3 == -INFINITY) ? 0.f : exp2f(l3 - M);
+    L += (w0 + w1) + (w2 + w3);
+    acc.x += w0 * v0.x + w1 * v1.x + w2 * v2.x + w3 * v3.x;
+    acc.y += w0 * v0.y + w1 * v1.y + w2 * v2.y + w3 * v3.y;
+    acc.z += w0 * v0.z + w1 * v1.z + w2 * v2.z + w3 * v3.z;
+    acc.w += w0 * v0.w + w1 * v1.w + w2 * v2.w + w3 * v3.w;
+  }
+  for (; i < n; i += MERGE_WARPS) add(i);
+  s_acc[warp][lane] = acc;
+  if (lane == 0) s_l[warp] = L;
+  __syncthreads();
+  if (warp != 0) return;
+  acc = s_acc[0][lane];
+  L = s_l[0];
+#pragma unroll
+  for (int w = 1; w < MERGE_WARPS; ++w) {
+    const float4 v = s_acc[w][lane];
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+    L += s_l[w];
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   const long long o = static_cast<long long>(b) * a.o_sb + static_cast<long long>(h) * a.o_sh + lane * 4;
@@ -779,10 +833,9 @@ __global__ void merge_kernel(const Args a) {
 }
 
 int launch(const Args& a, cudaStream_t stream) {
-  const int warps = a.B * a.H;
-  const int threads = 256;
-  const int blocks = (warps * 32 + threads - 1) / threads;
-  merge_kernel<<<blocks, threads, 0, stream>>>(a);
+  const long long blocks = static_cast<long long>(a.B) * a.H;
+  if (blocks > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
+  merge_kernel<<<static_cast<unsigned>(blocks), MERGE_WARPS * 32, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
 }
 

@@ -16,8 +16,12 @@ microbench/b1_bench_protocol.py:144-158). A step = one full prefill.
             workload, extrapolated by FLOP count; rank 0 only.
 
 Extra fields: window-off and k=64 prefill times, the on/off ratio against the
-2/(1+s) ceiling, and the windowed paged decode of BASELINE config 3 (batch 8,
-24/8 heads, 128K context, page 16) with its HBM roofline.
+2/(1+s) ceiling; the windowed paged decode of BASELINE config 3 (batch 8, 24/8
+heads, 8K/32K/128K context, page 16) with its HBM roofline (1 GPU); BASELINE
+config 5 (one 1M-token request, page 64, k=64 vs off) with the KV sequence
+split over the ranks, the NCCL all-gather of the partial (O, LSE) and the LSE
+merge inside each step; BASELINE config 4 (512K-token prefill, k=2, zig-zag
+over the ranks).
 """
 import argparse
 import json
@@ -250,6 +254,82 @@ def bench_decode(device, steps, warmup, peaks, N=131072):
     return res
 
 
+def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
+    """one 1M-token request, 28/4 heads, page 64, theta 1e7,
+    window k=64 vs off, the KV sequence split into `world` contiguous shards
+    (one per rank). Each step is this rank's split-KV decode over its shard,
+    the NCCL all-gather of the partial (O, LSE) and the LSE merge
+    (atflash.dist.sharded_decode); the time is the max over ranks."""
+    import atflash
+    from atflash import window_table as WT
+    B, hq, hkv, page = 1, 28, 4, 64
+    shard = N // world
+    npg = shard // page
+    g = torch.Generator(device="cpu").manual_seed(4242 + rank)
+    perm = torch.randperm(npg, generator=g).to(torch.int32)
+    gd = torch.Generator(device=device).manual_seed(77 + rank)
+    kc = torch.randn((npg, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    vc = torch.randn((npg, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    gq = torch.Generator(device=device).manual_seed(99)
+    q = torch.randn((B, hq, D), generator=gq, device=device).to(torch.bfloat16)
+    indptr = torch.tensor([0, npg], dtype=torch.int32)
+    lpl = torch.tensor([page], dtype=torch.int32)
+    q_pos = torch.tensor([N - 1], dtype=torch.int64, device=device)
+    kv_pos0 = torch.tensor([rank * shard], dtype=torch.int64, device=device)
+    ws = torch.empty(64 * 1024 * 1024, dtype=torch.uint8, device=device)
+    res = {}
+    for name, wt in (("on_k64", atflash.WindowTable(D, THETA, 64.0)), ("off", None)):
+        w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt)
+        ms, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0),
+                      steps, warmup, world)
+        zhi = wt.zhi16 if wt is not None else None
+        mine = WT.decode_bytes(hkv, [shard], zhi, q_pos=[N - 1 - rank * shard])["bytes"]
+        tot = torch.tensor([mine], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(tot)
+        total = float(tot.item())
+        agg = total / (ms * 1e-3) / 1e9
+        res[name] = {"us": ms * 1e3, "bytes_total": total, "gbs_aggregate": agg,
+                     "hbm_frac_per_gpu": agg / (world * peaks["hbm_gbs"])}
+    res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
+    res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, KV split into {world} shards, "
+                     "all-gather of (O, LSE) + LSE merge inside the step")
+    del kc, vc
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
+    """512K-token windowed prefill (k=2), 28/4 heads, zig-zag
+    query blocks over the ranks with K/V replicated; max-over-ranks ms."""
+    import atflash
+    from atflash import window_table as WT
+    g = torch.Generator(device=device).manual_seed(2027)
+    q = torch.randn((1, N, HQ, D), generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn((1, N, HKV, D), generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn((1, N, HKV, D), generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    wt = atflash.WindowTable(D, THETA, K_RET)
+    blocks = atflash.dist.zigzag_blocks(N, world, rank) if world > 1 else [(0, N)]
+
+    def fn(i):
+        for (s0, e0) in blocks:
+            if e0 > s0:
+                atflash.prefill_fwd(q[:, s0:e0], k[:, :e0], v[:, :e0], causal=True, window_table=wt,
+                                    q_offset=s0, out=out[:, s0:e0])
+    ms, _ = timed(fn, steps, warmup, world)
+    work = WT.prefill_work(HQ, N, N, wt.zhi16)
+    mine = sum(WT.prefill_work(HQ, e0 - s0, e0, wt.zhi16, q_offset=s0)["flops"] for (s0, e0) in blocks if e0 > s0)
+    res = {"ms": ms, "flops_total": work["flops"], "s": work["s"], "ceiling": work["ceiling"],
+           "tflops_this_rank": mine / (ms * 1e-3) / 1e12,
+           "frac_this_rank": mine / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+           "config": f"N={N}, k=2, zig-zag x{world}, K/V replicated"}
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -257,8 +337,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="atflash", choices=["atflash", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip off/k64/decode/e2e/cpu legs")
-    ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
-                    help="prefill: the headline leg alone; decode: the config-3 decode leg alone")
+    ap.add_argument("--only", default="all", choices=["all", "prefill", "decode", "decode1m", "prefill512k"],
+                    help="prefill: the headline leg alone; decode: the config-3 decode leg alone; "
+                         "decode1m / prefill512k: the config-5 / config-4 legs alone")
     ap.add_argument("--seq-len", type=int, default=131072,
                     help="sequence length (smaller values are for profiling captures)")
     args = ap.parse_args()
@@ -278,6 +359,14 @@ def main():
         res = bench_decode(device, args.steps, args.warmup, peaks, N=args.seq_len)
         if rank == 0:
             print(json.dumps({"decode": res}), flush=True)
+        return
+    if args.only in ("decode1m", "prefill512k"):
+        fn = bench_decode_1m if args.only == "decode1m" else bench_prefill_512k
+        res = fn(device, rank, world, args.steps, args.warmup, peaks)
+        if rank == 0:
+            print(json.dumps({args.only: res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
     inputs = prefill_inputs(device)
     wt2 = atflash.WindowTable(D, THETA, K_RET)
@@ -339,10 +428,15 @@ def main():
         e2e = {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         del qd, kd, vd
     decode = None
-    if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
+    decode_1m = None
+    prefill_512k = None
+    if not args.no_extras and args.only == "all":
         del inputs
         torch.cuda.empty_cache()
-        decode = bench_decode(device, 20, 5, peaks)
+        if world == 1:
+            decode = {f"{n // 1024}K": bench_decode(device, 20, 5, peaks, N=n) for n in (8192, 32768, 131072)}
+        decode_1m = bench_decode_1m(device, rank, world, 20, 5, peaks)
+        prefill_512k = bench_prefill_512k(device, rank, world, 2, 3, peaks)
     cpu = None
     if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
         cms, info = cpu_baseline_sample()
@@ -365,7 +459,8 @@ def main():
                            "l2": "inputs 1.2 GB per copy > 126 MB L2; two copies rotated"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
-                "device_error_flag": err, "extras": dict(extras, decode=decode) if extras else None}
+                "device_error_flag": err, "extras": dict(extras, decode=decode, decode_1m_sharded=decode_1m, prefill_512k=prefill_512k)
+                if extras else None}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -1,0 +1,124 @@
+"""Two-GPU runs of the sharded paths over NCCL (skipped with fewer than two GPUs).
+
+Zig-zag prefill: each rank computes its two query blocks against replicated
+K/V; the gathered rows must equal a one-GPU run bit for bit. KV-sharded decode:
+each rank decodes its contiguous shard of every request with global positions,
+the partial (O, LSE) are all-gathered and merged; the result must match the
+one-GPU decode of the whole cache (same kernels, different split points, so a
+tolerance rather than bit equality)."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, errq):
+    import datetime
+    import sys
+    import torch.distributed as dist
+    sys.path[:0] = [os.path.join(os.path.dirname(HERE), "atflash-kernel_b200")]
+    try:
+        import atflash
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        g = torch.Generator(device="cpu").manual_seed(31)
+        # --- zig-zag prefill
+        N, hq, hkv = 1536, 6, 2
+        q = torch.randn((1, N, hq, 128), generator=g).to(torch.bfloat16).to(dev)
+        k = torch.randn((1, N, hkv, 128), generator=g).to(torch.bfloat16).to(dev)
+        v = torch.randn((1, N, hkv, 128), generator=g).to(torch.bfloat16).to(dev)
+        wt = atflash.WindowTable(128, 1e4, 2.0)
+        full = atflash.dist.sharded_prefill(q, k, v, window_table=wt, gather=True)
+        single = atflash.prefill_fwd(q, k, v, causal=True, window_table=wt)
+        torch.cuda.synchronize()
+        assert torch.equal(full, single), "zig-zag rows differ from the one-GPU run"
+        # --- KV-sharded decode: 3 requests, page 16, every rank holds a contiguous key range
+        lens = [4096, 2048, 1040]
+        page, hq, hkv = 16, 24, 8
+        qd = torch.randn((len(lens), hq, 128), generator=g).to(torch.bfloat16).to(dev)
+        ks = [torch.randn((n, hkv, 128), generator=g).to(torch.bfloat16) for n in lens]
+        vs = [torch.randn((n, hkv, 128), generator=g).to(torch.bfloat16) for n in lens]
+
+        def paged(kl, vl):
+            pages, indptr, lpl, kp, vp = [], [0], [], [], []
+            for kk, vv in zip(kl, vl):
+                n = kk.shape[0]
+                npg = (n + page - 1) // page
+                pad = npg * page - n
+                kk = torch.cat([kk, kk.new_zeros((pad, hkv, 128))]).view(npg, page, hkv, 128)
+                vv = torch.cat([vv, vv.new_zeros((pad, hkv, 128))]).view(npg, page, hkv, 128)
+                kp.append(kk)
+                vp.append(vv)
+                indptr.append(indptr[-1] + npg)
+                lpl.append(n - (npg - 1) * page)
+            kc = torch.cat(kp).to(dev)
+            vc = torch.cat(vp).to(dev)
+            idx = torch.arange(indptr[-1], dtype=torch.int32)
+            return kc, vc, torch.tensor(indptr, dtype=torch.int32), idx, torch.tensor(lpl, dtype=torch.int32)
+
+        ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+        kc, vc, indptr, idx, lpl = paged(ks, vs)
+        w1 = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        w1.plan(indptr, idx, lpl, hq, hkv, 128, page, window_table=wt)
+        ref = w1.run(qd, (kc, vc), out_dtype=torch.float32)
+        # this rank's contiguous shard of every request, cut at page boundaries
+        kl, vl, pos0 = [], [], []
+        for kk, vv, n in zip(ks, vs, lens):
+            npg = (n + page - 1) // page
+            cut = [min(n, ((npg * r) // world) * page) for r in range(world + 1)]
+            kl.append(kk[cut[rank]:cut[rank + 1]])
+            vl.append(vv[cut[rank]:cut[rank + 1]])
+            pos0.append(cut[rank])
+        assert all(x.shape[0] > 0 for x in kl)
+        kc2, vc2, indptr2, idx2, lpl2 = paged(kl, vl)
+        ws2 = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+        w2 = atflash.BatchDecodeWithPagedKVCacheWrapper(ws2, "NHD")
+        w2.plan(indptr2, idx2, lpl2, hq, hkv, 128, page, window_table=wt)
+        q_pos = torch.tensor([n - 1 for n in lens], dtype=torch.int64, device=dev)
+        kv_pos0 = torch.tensor(pos0, dtype=torch.int64, device=dev)
+        out, lse = atflash.dist.sharded_decode(qd, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                               out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        err = (out - ref).abs().max().item()
+        assert err < 2e-3, f"sharded decode differs from the one-GPU decode by {err}"
+        assert atflash.check_device_errors() == 0
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, which fails the test
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_two_gpu_zigzag_prefill_and_sharded_decode():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    msgs = []
+    while not errq.empty():
+        msgs.append(errq.get())
+    assert not msgs, "; ".join(msgs)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
