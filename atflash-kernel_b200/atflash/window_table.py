@@ -46,6 +46,34 @@ def wavelengths_sorted(head_dim: int, rope_base: float, k_ret: float, device="cp
     return torch.tensor(_widths_list(head_dim, rope_base, k_ret), dtype=torch.float32, device=device)
 
 
+def wavelengths_from_inv_freq(inv_freq, k_ret: float, device="cpu") -> torch.Tensor:
+    """fp32 [P]: window widths from a model's own RoPE inv_freq (rope scaling such
+    as YaRN or Llama-3 included), sorted descending.
+
+    w_r = k * (2*pi / inv_freq_r) in fp64, rounded to fp32: the reference's
+    "entity" tables (window_tables/w_meta_from_hf.py:28-30,
+    window_tables/w_meta_7b1m_yarn_s2.py:35-37). k_ret = inf gives +inf."""
+    inv = [float(x) for x in (inv_freq.detach().double().cpu().tolist()
+                              if isinstance(inv_freq, torch.Tensor) else inv_freq)]
+    if math.isinf(k_ret):
+        w = [float("inf")] * len(inv)
+    else:
+        w = [_f32(float(k_ret) * (2.0 * math.pi / f)) for f in inv]
+    return torch.tensor(sorted(w, reverse=True), dtype=torch.float32, device=device)
+
+
+def pair_order_from_inv_freq(inv_freq) -> Tuple[List[int], bool]:
+    """RoPE pairs r in order of descending wavelength 2*pi/inv_freq_r, and whether
+    that is the canonical order r = P-1, ..., 0 that the sorted-pair layout and
+    the kernels' rotate_half level map assume. The reference's harness stops
+    when it is not (e2e_pipeline/atflash_e2e_fafi.py:143-157)."""
+    inv = [float(x) for x in (inv_freq.detach().double().cpu().tolist()
+                              if isinstance(inv_freq, torch.Tensor) else inv_freq)]
+    lam = [2.0 * math.pi / f for f in inv]
+    order = sorted(range(len(lam)), key=lambda r: (-lam[r], r))
+    return order, order == list(range(len(lam) - 1, -1, -1))
+
+
 def _as_list(wvec) -> List[float]:
     if isinstance(wvec, torch.Tensor):
         return [float(x) for x in wvec.detach().to("cpu", torch.float32).tolist()]
@@ -147,9 +175,10 @@ def mma_slice_stats(phase: str, m_ctx: int, n_ctx: int, block_m: int, block_n: i
             "qk_slice_ratio": tw / max(1, tf), "kload_dim_ratio": tw / max(1, tf)}
 
 
-def zhi_slice_vec8(head_dim: int, rope_base: float, k_ret: float, device="cuda:0") -> torch.Tensor:
-    """int32 [d/8]: largest distance at which 8-dim slice tx is read (floor(w[4 tx]))."""
-    w = _widths_list(head_dim, rope_base, k_ret)
+def zhi_slice_vec8(head_dim: int, rope_base: float, k_ret: float, device="cuda:0", widths=None) -> torch.Tensor:
+    """int32 [d/8]: largest distance at which 8-dim slice tx is read (floor(w[4 tx])).
+    ``widths`` (sorted descending) replaces the base/k formula when given."""
+    w = sorted(_as_list(widths), reverse=True) if widths is not None else _widths_list(head_dim, rope_base, k_ret)
     out = []
     for tx in range(head_dim // 8):
         x = w[4 * tx]
@@ -235,20 +264,40 @@ class WindowTable:
     """A model's window: head_dim, RoPE base and the number of retained periods k.
 
     ``zhi16`` (cap = every distance) is what the kernels consume; ``wvec`` is the
-    fp32 width vector the reference's oracle takes."""
+    fp32 width vector the reference's oracle takes. ``widths`` (fp32, sorted
+    descending) overrides the base/k formula: ``WindowTable.from_inv_freq`` sets
+    it from a model's own (possibly scaled) RoPE frequencies."""
     head_dim: int
     rope_base: float
     k_ret: float
+    widths: Union[Tuple[float, ...], None] = None
     _cache: Dict[int, Tuple[int, ...]] = field(default_factory=dict, repr=False)
+
+    @classmethod
+    def from_inv_freq(cls, inv_freq, k_ret: float, rope_base: float = float("nan"),
+                      require_canonical_order: bool = True) -> "WindowTable":
+        """Window from a model's RoPE inv_freq (e.g. ``model.model.rotary_emb.inv_freq``,
+        YaRN / Llama-3 scaling included). The kernels assume the canonical pair
+        order (wavelength growing with r); a model that breaks it raises."""
+        order, canonical = pair_order_from_inv_freq(inv_freq)
+        if require_canonical_order and not canonical:
+            raise ValueError(f"inv_freq is not in canonical order (longest wavelengths first: {order[:8]})")
+        w = wavelengths_from_inv_freq(inv_freq, k_ret)
+        return cls(head_dim=2 * w.numel(), rope_base=rope_base, k_ret=float(k_ret),
+                   widths=tuple(float(x) for x in w.tolist()))
+
+    def _widths(self) -> List[float]:
+        if self.widths is not None:
+            return list(self.widths)
+        return _widths_list(self.head_dim, self.rope_base, self.k_ret)
 
     @property
     def wvec(self) -> torch.Tensor:
-        return wavelengths_sorted(self.head_dim, self.rope_base, self.k_ret)
+        return torch.tensor(self._widths(), dtype=torch.float32)
 
     def zhi(self, n_ctx: int = KERNEL_CAP) -> Tuple[int, ...]:
         if n_ctx not in self._cache:
-            self._cache[n_ctx] = zhi_table(_widths_list(self.head_dim, self.rope_base, self.k_ret),
-                                           self.head_dim, n_ctx)
+            self._cache[n_ctx] = zhi_table(self._widths(), self.head_dim, n_ctx)
         return self._cache[n_ctx]
 
     @property
@@ -257,7 +306,8 @@ class WindowTable:
 
     @property
     def zhi8(self) -> List[int]:
-        return zhi_slice_vec8(self.head_dim, self.rope_base, self.k_ret, device="cpu").tolist()
+        return zhi_slice_vec8(self.head_dim, self.rope_base, self.k_ret, device="cpu",
+                              widths=self.widths).tolist()
 
     @property
     def enabled(self) -> bool:

@@ -8,6 +8,10 @@ tests never need the reference at run time:
     python tests/golden/make_golden.py --reference /root/reference
 
 What is recorded, all produced by the reference's own code:
+  w_meta_tables.json  the reference's recorded RoPE-scaled window inputs
+                      (window_tables/w_meta_*.json: a model's own inv_freq and
+                      the widths k * 2*pi / inv_freq) with the zhi levels the
+                      reference's zhi_table gives for them.
   window_tables.json  atflash/window_table.py (torch) and the torch-free twin
                       window_tables/atflash_window.py: fp32 widths (bit patterns),
                       D_eff at many distances, zhi levels (16-snap) at three caps,
@@ -134,6 +138,24 @@ def main():
         json.dump({"generator": "tests/golden/make_golden.py", "tables": tables, "stats": stats,
                    "c1_recorded": {"model": "Qwen2.5-7B-Instruct-1M", "base": 1e7, "head_dim": 128,
                                    "cap": 1_100_000, "tables": c1}}, f, indent=0)
+
+    # RoPE-scaled ("entity") window tables: the reference's recorded inv_freq and
+    # widths (window_tables/w_meta_*.json, made by w_meta_from_hf.py and
+    # w_meta_7b1m_yarn_s2.py) and the reference's zhi levels of those widths
+    wmeta = []
+    for fn in sorted(os.listdir(os.path.join(ref, "window_tables"))):
+        if not (fn.startswith("w_meta_") and fn.endswith(".json")):
+            continue
+        m = json.load(open(os.path.join(ref, "window_tables", fn)))
+        d = 2 * len(m["inv_freq"])
+        w_sorted32 = sorted((struct.unpack("<f", struct.pack("<f", x))[0] for x in m["w"]), reverse=True)
+        wmeta.append({"source": fn, "model": m["model"], "k": m["k_convex"],
+                      "rope_scaling": m.get("rope_scaling"), "head_dim": d,
+                      "inv_freq": m["inv_freq"], "w_fp64": m["w"],
+                      "w_sorted_fp32_bits": [f32_bits(x) for x in w_sorted32],
+                      "zhi16": {str(c): list(AW.zhi_table(w_sorted32, d, c)) for c in CAPS}})
+    with open(os.path.join(HERE, "w_meta_tables.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py", "tables": wmeta}, f, indent=0)
 
     meta = {"prefill": [], "decode": []}
     d = 128

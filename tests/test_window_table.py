@@ -140,3 +140,49 @@ def test_c_abi_tables_match_reference():
         z8 = (ctypes.c_int32 * (d // 8))()
         assert lib.atf_window_zhi8(buf, d, z8) == 0
         assert list(z8) == rec["zhi8"]
+
+
+# ------------------------------------------------------- RoPE-scaled (entity) tables
+def _wmeta():
+    import json
+    return json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                                       "w_meta_tables.json")))["tables"]
+
+
+def test_widths_from_inv_freq_match_reference_entity_tables():
+    """k * 2*pi / inv_freq in fp64, rounded to fp32 and sorted, bit for bit as the
+    reference's recorded tables (base model and YaRN s=2 included)."""
+    import struct
+    from atflash import window_table as WT
+    tabs = _wmeta()
+    assert len(tabs) == 3 and any(t["rope_scaling"] for t in tabs)
+    for t in tabs:
+        w = WT.wavelengths_from_inv_freq(t["inv_freq"], t["k"])
+        bits = [struct.unpack("<I", struct.pack("<f", x))[0] for x in w.tolist()]
+        assert bits == t["w_sorted_fp32_bits"], t["source"]
+
+
+def test_window_table_from_inv_freq_levels_match_reference():
+    from atflash import window_table as WT
+    for t in _wmeta():
+        wt = WT.WindowTable.from_inv_freq(t["inv_freq"], t["k"])
+        assert wt.head_dim == t["head_dim"]
+        for cap, zhi in t["zhi16"].items():
+            assert list(wt.zhi(int(cap))) == zhi, (t["source"], cap)
+        # the kernel table covers every distance and agrees with D_eff of the widths
+        for z in (0, 1, 100, 10_000, 1_000_000):
+            assert wt.deff(z) == WT.deff_of_zmin(z, wt.wvec, wt.head_dim)
+
+
+def test_pair_order_gate():
+    """The reference's harness stops unless the model's wavelengths grow with the
+    pair index (e2e_pipeline/atflash_e2e_fafi.py:143-157); so does from_inv_freq."""
+    from atflash import window_table as WT
+    for t in _wmeta():
+        order, canonical = WT.pair_order_from_inv_freq(t["inv_freq"])
+        assert canonical and order[0] == len(t["inv_freq"]) - 1
+    inv = list(_wmeta()[0]["inv_freq"])
+    inv[3], inv[7] = inv[7], inv[3]
+    assert not WT.pair_order_from_inv_freq(inv)[1]
+    with pytest.raises(ValueError):
+        WT.WindowTable.from_inv_freq(inv, 2.0)
