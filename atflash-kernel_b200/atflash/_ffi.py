@@ -21,7 +21,8 @@ ATF_NOALLOC_MAX_PARTIAL_ROWS = 16384
 
 EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_window_deff",
             "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
-            "atf_rope_pack", "atf_status_string", "atf_version", "atf_read_error_flag")
+            "atf_rope_pack", "atf_paged_kv_append", "atf_status_string", "atf_version",
+            "atf_read_error_flag")
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
 
@@ -82,6 +83,16 @@ class AtfRopeParams(ctypes.Structure):
                 ("positions", _vp), ("pos_offset", _i64), ("out_layout", ctypes.c_int)]
 
 
+class AtfAppendParams(ctypes.Structure):
+    _fields_ = [("append_k", _vp), ("append_v", _vp), ("nnz", _i64), ("a_stride_n", _i64), ("a_stride_h", _i64),
+                ("batch_indices", _vp), ("positions", _vp), ("k_cache", _vp), ("v_cache", _vp),
+                ("num_pages", _i64), ("kv_stride_page", _i64), ("kv_stride_token", _i64),
+                ("kv_stride_head", _i64), ("num_kv_heads", _i32), ("head_dim", _i32), ("page_size", _i32),
+                ("batch_size", _i32), ("kv_indptr", _vp), ("kv_indices", _vp), ("cos", _vp), ("sin", _vp),
+                ("cs_stride_pos", _i64), ("n_pos", _i64), ("rope_positions", _vp), ("out_layout", ctypes.c_int),
+                ("error_flag", _vp)]
+
+
 class AtfError(RuntimeError):
     """A non-zero status from the C ABI."""
 
@@ -116,6 +127,7 @@ def load() -> ctypes.CDLL:
             lib.atf_decode_run_noalloc.argtypes = [P(AtfDecodeParams), _vp]
             lib.atf_lse_merge.argtypes = [P(AtfMergeParams), _vp]
             lib.atf_rope_pack.argtypes = [P(AtfRopeParams), _vp]
+            lib.atf_paged_kv_append.argtypes = [P(AtfAppendParams), _vp]
             lib.atf_status_string.argtypes = [ctypes.c_int]
             lib.atf_status_string.restype = ctypes.c_char_p
             lib.atf_read_error_flag.argtypes = [_vp, P(ctypes.c_int)]

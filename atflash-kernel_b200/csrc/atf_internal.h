@@ -11,6 +11,8 @@ namespace atf {
 
 // Error code a bounded device wait writes to the caller's error flag.
 constexpr int kDevErrTimeout = 1;
+// Error code the paged-KV append writes for a token whose page index is out of range.
+constexpr int kDevErrIndex = 2;
 
 // Encodes a tiled TMA descriptor through the driver entry point (loaded once).
 // dims / strides are innermost first; strides are in bytes for dims 1..rank-1.

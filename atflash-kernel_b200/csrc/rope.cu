@@ -1,18 +1,13 @@
 // Fused RoPE + pair-order pack: pre-RoPE bf16 q or k in HF rotate_half order
-// -> post-RoPE bf16 in rotate_half or wavelength-sorted pair order.
-//
-// Arithmetic follows the reference's test front-end
-// (microbench/b1_correctness.py:113-123): out1 = x1*cos - x2*sin and
-// out2 = x2*cos + x1*sin in fp32 with separately rounded products (no FMA
-// contraction), then round-to-nearest-even to bf16. The sorted-pair order is
-// hf_to_sorted_pair_perm (microbench/b1_correctness.py:126-135): sorted pair j
-// = HF pair r = P-1-j at dims (2j, 2j+1).
+// -> post-RoPE bf16 in rotate_half or wavelength-sorted pair order (the
+// arithmetic and the pair order are in rope_math.cuh).
 //
 // Thread = one (token, head, chunk c in 0..7): reads HF dims [8c, 8c+8) and
 // [64+8c, 64+8c+8) (16 B each) plus 8 cos and 8 sin values. In sorted order
 // those 8 pairs are the contiguous 32 B at dims [16(7-c), 16(7-c)+16), pair
 // order reversed.
 #include "atf_internal.h"
+#include "rope_math.cuh"
 
 namespace atf {
 namespace rope {
@@ -30,8 +25,6 @@ struct Args {
   int sorted;
 };
 
-__device__ __forceinline__ float bf2f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
-
 __global__ void rope_kernel(const Args a) {
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = a.B * a.S * a.H * 8;
@@ -46,41 +39,8 @@ __global__ void rope_kernel(const Args a) {
   if (pos < 0) pos = 0;
   if (pos >= a.n_pos) pos = a.n_pos - 1;
   const __nv_bfloat16* xr = a.x + b * a.xs_b + s * a.xs_s + h * a.xs_h;
-  const uint4 lo = *reinterpret_cast<const uint4*>(xr + 8 * c);
-  const uint4 hi = *reinterpret_cast<const uint4*>(xr + 64 + 8 * c);
-  const float* cr = a.cs + pos * a.cs_stride + 8 * c;
-  const float* sr = a.sn + pos * a.cs_stride + 8 * c;
-  const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
-  const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
-  float r1[8], r2[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float x1 = bf2f((lw[e >> 1] >> (16 * (e & 1))) & 0xffffu);
-    const float x2 = bf2f((hw[e >> 1] >> (16 * (e & 1))) & 0xffffu);
-    const float cv = cr[e], sv = sr[e];
-    r1[e] = __fsub_rn(__fmul_rn(x1, cv), __fmul_rn(x2, sv));
-    r2[e] = __fadd_rn(__fmul_rn(x2, cv), __fmul_rn(x1, sv));
-  }
   __nv_bfloat16* orow = a.out + b * a.os_b + s * a.os_s + h * a.os_h;
-  auto pk = [](float l, float h2) -> uint32_t {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(l, h2);  // .x = low half
-    return *reinterpret_cast<const uint32_t*>(&v);
-  };
-  if (!a.sorted) {
-    uint4 o1, o2;
-    o1.x = pk(r1[0], r1[1]); o1.y = pk(r1[2], r1[3]); o1.z = pk(r1[4], r1[5]); o1.w = pk(r1[6], r1[7]);
-    o2.x = pk(r2[0], r2[1]); o2.y = pk(r2[2], r2[3]); o2.z = pk(r2[4], r2[5]); o2.w = pk(r2[6], r2[7]);
-    *reinterpret_cast<uint4*>(orow + 8 * c) = o1;
-    *reinterpret_cast<uint4*>(orow + 64 + 8 * c) = o2;
-  } else {
-    // sorted pair j_local = 0..7 within the block <- HF pair r = 8c + 7 - j_local
-    uint32_t w[8];
-#pragma unroll
-    for (int jl = 0; jl < 8; ++jl) w[jl] = pk(r1[7 - jl], r2[7 - jl]);
-    uint4* dst = reinterpret_cast<uint4*>(orow + 16 * (7 - c));
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-  }
+  ropemath::rotate_chunk(xr, a.cs + pos * a.cs_stride, a.sn + pos * a.cs_stride, orow, c, a.sorted != 0);
 }
 
 }  // namespace rope

@@ -246,6 +246,37 @@ typedef struct {
  * contraction), rounded to bf16, written in the requested pair order. */
 int atf_rope_pack(const AtfRopeParams* p, atf_stream_t stream);
 
+/* ------------------------------------------------------------------ paged-KV append */
+
+typedef struct {
+  const void* append_k; /* bf16 [nnz, Hkv, 128]: pre-RoPE HF rotate_half order when cos/sin are given */
+  const void* append_v; /* bf16 [nnz, Hkv, 128] */
+  int64_t nnz;
+  int64_t a_stride_n, a_stride_h; /* same for append_k and append_v */
+  const int32_t* batch_indices;   /* device [nnz]: request of each token */
+  const int32_t* positions;       /* device [nnz]: position of the token in its request's KV */
+  void* k_cache;                  /* bf16 pages, NHD [P, page, Hkv, 128] or HND [P, Hkv, page, 128] */
+  void* v_cache;
+  int64_t num_pages;
+  int64_t kv_stride_page, kv_stride_token, kv_stride_head;
+  int32_t num_kv_heads, head_dim, page_size, batch_size;
+  const int32_t* kv_indptr;       /* device [B+1] */
+  const int32_t* kv_indices;      /* device page ids */
+  const float* cos;               /* optional fp32 [n_pos, >=64]: rotate K at write */
+  const float* sin;
+  int64_t cs_stride_pos, n_pos;
+  const int64_t* rope_positions;  /* optional device [nnz]: RoPE position (default: positions[i]) */
+  int out_layout;                 /* with RoPE: pair order written (ATF_LAYOUT_*) */
+  int* error_flag;                /* optional: set to 2 when a token's page index is out of range */
+} AtfAppendParams;
+
+/* Append K/V tokens to a paged cache: token i goes to page
+ * kv_indices[kv_indptr[b] + pos / page], slot pos % page (b = batch_indices[i],
+ * pos = positions[i]); with cos/sin, K is rotated and packed into out_layout.
+ * Replaces FlashInfer's append_paged_kv_cache, which feeds the reference's
+ * decode (e2e_pipeline/atflash_e2e_fafi.py:219-223). */
+int atf_paged_kv_append(const AtfAppendParams* p, atf_stream_t stream);
+
 /* ------------------------------------------------------------------ misc */
 
 const char* atf_status_string(int status);

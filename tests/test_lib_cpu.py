@@ -123,3 +123,21 @@ def test_decode_plan_rejects_bad_tables():
     pp.num_qo_heads = 8 * 17  # group of 17 > 16
     lpl[0] = 3
     assert lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)) == -2
+
+
+def test_append_rejects_bad_arguments_without_gpu():
+    from atflash import _ffi
+    lib = _lib()
+    assert lib.atf_paged_kv_append(None, None) == -1
+    p = _ffi.AtfAppendParams()
+    assert lib.atf_paged_kv_append(ctypes.byref(p), None) == -1  # null tensors
+    p.append_k = p.append_v = p.batch_indices = p.positions = 256
+    p.k_cache = p.v_cache = p.kv_indptr = p.kv_indices = 256
+    p.head_dim, p.num_kv_heads, p.page_size, p.batch_size, p.num_pages = 64, 1, 16, 1, 1
+    assert lib.atf_paged_kv_append(ctypes.byref(p), None) == -2  # head_dim 64
+    p.head_dim = 128
+    p.cos = 256  # cos without sin
+    assert lib.atf_paged_kv_append(ctypes.byref(p), None) == -1
+    p.cos = None
+    p.a_stride_n = 3  # misaligned token stride
+    assert lib.atf_paged_kv_append(ctypes.byref(p), None) == -3
