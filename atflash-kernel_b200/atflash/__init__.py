@@ -11,6 +11,7 @@
     append_paged_kv_cache
                    write new K/V tokens into a paged cache (RoPE + pack on K)
     dist           zig-zag sharded prefill and KV-sharded decode over torch.distributed
+    hf             transformers AttentionInterface function (import atflash.hf)
 
 All compute runs in libatflash_b200.so through its C ABI (include/atflash_b200.h);
 there is no CPU path.
