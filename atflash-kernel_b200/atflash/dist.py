@@ -134,6 +134,11 @@ def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Ten
     """Decode with this rank's KV shard; `wrapper` is planned over the rank's local
     pages. q_pos: global query position per request; kv_pos0: global position of
     this rank's first key per request. Returns (out, lse) merged over the group."""
+    _, world = _rank_world(group)
+    if world == 1:
+        # one shard: the decode's own split merge is already the result
+        return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                           out_dtype=out_dtype)
     o, lse = wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
                          out_dtype=torch.float32)
     return merge_partials(o, lse, group=group, out_dtype=out_dtype)

@@ -46,6 +46,67 @@
 namespace atf {
 namespace prefill {
 
+// MMA groups are issued from one asm block each, under a single elect: the MMA
+// warp shares its sub-partition with two softmax warps, so fewer instructions
+// per tcgen05.mma keep the tensor pipe fed.
+//
+// one elected lane issues the 8 PV MMAs (K = 128 keys) of a tile and the commit
+__device__ __forceinline__ void pv_group_asm(uint32_t o_tmem, uint32_t p_tmem, uint64_t vd, uint32_t idesc,
+                                             uint32_t acc0, uint32_t bar_addr) {
+  asm volatile(
+      "{\n\t.reg .pred pe, pa;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+      "elect.sync _|pe, 0xffffffff;\n\t"
+      "setp.ne.b32 pa, %4, 0;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pa;\n\t"
+      "add.u32 a, %1, 8;\n\tadd.u64 b, %2, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "add.u32 a, a, 8;\n\tadd.u64 b, b, 128;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, 1;\n\t"
+      "@pe tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+      ::"r"(o_tmem), "r"(p_tmem), "l"(vd), "r"(idesc), "r"(acc0), "r"(bar_addr)
+      : "memory");
+}
+// one elected lane issues the L (1..8) QK MMAs of a tile and the commit; level
+// i advances A by 4 KB and B by 4 KB (descriptor start field += 256)
+__device__ __forceinline__ void qk_group_asm(uint32_t d_tmem, uint64_t qd, uint64_t kd, uint32_t idesc, int L,
+                                             uint32_t bar_addr) {
+  asm volatile(
+      "{\n\t.reg .pred pe, p1, p2, p3, p4, p5, p6, p7;\n\t.reg .b64 a, b;\n\t"
+      "elect.sync _|pe, 0xffffffff;\n\t"
+      "setp.gt.and.s32 p1, %4, 1, pe;\n\tsetp.gt.and.s32 p2, %4, 2, pe;\n\tsetp.gt.and.s32 p3, %4, 3, pe;\n\t"
+      "setp.gt.and.s32 p4, %4, 4, pe;\n\tsetp.gt.and.s32 p5, %4, 5, pe;\n\tsetp.gt.and.s32 p6, %4, 6, pe;\n\t"
+      "setp.gt.and.s32 p7, %4, 7, pe;\n\t"
+      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n\t"
+      "add.u64 a, %1, 256;\n\tadd.u64 b, %2, 256;\n\t"
+      "@p1 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p3 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p4 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p5 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p6 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "add.u64 a, a, 256;\n\tadd.u64 b, b, 256;\n\t"
+      "@p7 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
+      "@pe tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+      ::"r"(d_tmem), "l"(qd), "l"(kd), "r"(idesc), "r"(L), "r"(bar_addr)
+      : "memory");
+}
+
+
 constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
 constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
 constexpr uint32_t QHALF_BYTES = BM * 16;             // 2 KB
@@ -274,20 +335,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
       const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
       const uint64_t kd = kdesc0 + (((j % KST) * KSTAGE_BYTES) >> 4);
-      for (int i = 0; i < L; ++i)
-        mma_ss_elect(d_tmem, qd + ((i * QSLAB_BYTES) >> 4), kd + ((i * KSLAB_BYTES) >> 4), IDESC_QK,
-                     i > 0 ? 1u : 0u);
-      tc_commit_elect(bar(B_SFULL + t));
+      qk_group_asm(d_tmem, qd, kd, IDESC_QK, L, bar(B_SFULL + t));
     };
     auto issue_PV = [&](int t, int j) {
       const uint32_t o_tmem = tm + 256u + static_cast<uint32_t>(t * 128);
       const uint32_t p_tmem = tm + static_cast<uint32_t>(t * 128);
       const uint64_t vd = vdesc0 + (((j % VST) * VSTAGE_BYTES) >> 4);
-#pragma unroll
-      for (int c = 0; c < BN / 16; ++c)
-        mma_ts_elect(o_tmem, p_tmem + static_cast<uint32_t>(c * 8), vd + ((c * 2048) >> 4), IDESC_PV,
-                     (j > 0 || c > 0) ? 1u : 0u);
-      tc_commit_elect(bar(B_ODONE + t));
+      pv_group_asm(o_tmem, p_tmem, vd, IDESC_PV, j > 0 ? 1u : 0u, bar(B_ODONE + t));
     };
     bool ok = __all_sync(FULL, mbar_wait(bar(B_Q), 0, ab, kDevErrTimeout));
     tc_fence_after();
