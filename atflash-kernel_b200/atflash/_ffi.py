@@ -22,7 +22,7 @@ ATF_NOALLOC_MAX_PARTIAL_ROWS = 16384
 EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_window_deff",
             "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
             "atf_rope_pack", "atf_paged_kv_append", "atf_status_string", "atf_version",
-            "atf_read_error_flag")
+            "atf_read_error_flag", "atf_selftest_wait_timeout")
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
 
@@ -131,6 +131,7 @@ def load() -> ctypes.CDLL:
             lib.atf_status_string.argtypes = [ctypes.c_int]
             lib.atf_status_string.restype = ctypes.c_char_p
             lib.atf_read_error_flag.argtypes = [_vp, P(ctypes.c_int)]
+            lib.atf_selftest_wait_timeout.argtypes = [_vp, _vp]
             for name in EXPORTED:
                 if name not in ("atf_status_string",):
                     getattr(lib, name).restype = ctypes.c_int

@@ -49,3 +49,15 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
         elif t.device != dev:
             raise ValueError("all tensors must be on the same device")
     return dev
+
+
+def selftest_wait_timeout(device=None) -> int:
+    """Run the bounded-wait self-test on `device` (about 2 s): a kernel waits on
+    a barrier nothing arrives on, gives up after the wait limit and reports
+    through the error flag. Returns the flag value (1 = wait timed out)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flag = error_flag(dev)
+    with torch.cuda.device(dev):
+        _ffi.check("atf_selftest_wait_timeout",
+                   _ffi.load().atf_selftest_wait_timeout(flag.data_ptr(), stream_handle(dev)))
+    return check_device_errors(dev)

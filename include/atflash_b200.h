@@ -284,6 +284,13 @@ int atf_version(void);
 /* Synchronises the current device, copies *error_flag to *out and clears it. */
 int atf_read_error_flag(int* error_flag_device, int* out);
 
+/* Self-test of the bounded device waits (no counterpart in the reference, which
+ * has no device-side waits): launches one thread that waits on an mbarrier that
+ * nothing arrives on. After the wait limit (2 s) the kernel writes 1 to
+ * *error_flag and returns; the context stays usable. Failure detection is
+ * tested this way instead of with a fault. */
+int atf_selftest_wait_timeout(int* error_flag_device, atf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -143,3 +143,44 @@ def test_gloo_two_ranks_sharded_prefill_and_decode_merge():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(results) == {0: (True, True), 1: (True, True)}
+
+
+def _worker_lost_peer(rank, world, port, results):
+    """Rank 1 leaves before the decode merge's all-gather; rank 0 must get an
+    error from the collective within the process-group timeout, not hang."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        results[rank] = "left"
+        os._exit(0)  # leaves between steps, with no collective in flight
+    o = torch.zeros((1, 4, 128))
+    lse = torch.zeros((1, 4))
+    t0 = time.time()
+    try:
+        AD.merge_partials(o, lse, merge_fn=lambda po, pl: (po[0], pl[0]))
+        results[rank] = "no error"
+    except Exception as e:  # gloo reports the lost peer or the timeout
+        results[rank] = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
+
+
+def test_gloo_lost_rank_fails_the_collective_within_the_timeout():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    procs = [ctx.Process(target=_worker_lost_peer, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert results.get(1) == "left"
+    msg = results.get(0, "hung")
+    assert msg.startswith("error after"), msg
+    assert float(msg.split()[2].rstrip("s:")) < 60, msg
