@@ -41,10 +41,15 @@ class BatchDecodeWithPagedKVCacheWrapper:
         self._ws = float_workspace_buffer
         self._kv_layout = kv_layout
         self._plan = None
+        self._use_cuda_graph = bool(use_cuda_graph)
 
     @property
     def is_cuda_graph_enabled(self) -> bool:
-        return False
+        """True when built with use_cuda_graph: run() may then be captured in a
+        CUDA graph and replayed, with the plan and the q / cache / out buffers
+        fixed (the tables live on the device and run() neither allocates nor
+        synchronises when out is given)."""
+        return self._use_cuda_graph
 
     def reset_workspace_buffer(self, float_workspace_buffer, int_workspace_buffer=None):
         self._ws = float_workspace_buffer
