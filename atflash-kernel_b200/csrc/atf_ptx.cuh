@@ -327,56 +327,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Packed fp32 pairs (f32x2 ops): one instruction for two lanes of work.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-
-// 2^x for a pair on the FMA pipe (no MUFU), x in [-126, 8] (clamped below).
-// Cody-Waite range reduction (W. J. Cody and W. Waite, "Software Manual for
-// the Elementary Functions", 1980): x = n + f with n = round(x) obtained by
-// adding and subtracting 1.5*2^23, f in [-0.5, 0.5]; 2^f by a degree-3
-// polynomial whose coefficients are a relative-error minimax (Remez) fit on
-// [-0.5, 0.5] (max relative error 7.5e-5, ample for bf16 probabilities);
-// 2^n is added to the exponent field. Inputs below -126 give ~1e-38, not 0,
-// so masked (-inf) entries must not take this path.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kMagic = 12582912.0f;
-  constexpr float c0 = 0.99992805719375610f, c1 = 0.69326096773147583f;
-  constexpr float c2 = 0.24261112511157990f, c3 = 0.05517166852951050f;
-  x.x = fmaxf(x.x, -126.0f);
-  x.y = fmaxf(x.y, -126.0f);
-  const float2 y = fadd2(x, make_float2(kMagic, kMagic));
-  const float2 n = fadd2(y, make_float2(-kMagic, -kMagic));
-  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
-  float2 p = ffma2(make_float2(c3, c3), f, make_float2(c2, c2));
-  p = ffma2(p, f, make_float2(c1, c1));
-  p = ffma2(p, f, make_float2(c0, c0));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(y.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(y.y) << 23)));
-}
-
 // lo goes to the low 16 bits, hi to the high 16 bits.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t d;
