@@ -238,3 +238,32 @@ def test_prefill_full_size_sampled_tiles(cuda_device):
             got = out[:, t * 128:hi, h:h + 1].transpose(1, 2).float().cpu().numpy()
             mx, mean = err_stats(got, ref)
             assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (t, h, mx, mean)
+
+
+def test_prefill_512k_sampled_tiles(cuda_device):
+    """BASELINE config 4 shape (N = 524288, 28/4/128, theta 1e7, k=2): every
+    output row of two sampled query tiles (middle, last) of two heads against
+    the oracle, as the reference checks large N on a subset (head-subset parity)."""
+    atflash = _atf()
+    N, hq, hkv = 524288, 28, 4
+    g = torch.Generator(device=cuda_device).manual_seed(2027)
+    q = torch.randn((1, N, hq, 128), generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn((1, N, hkv, 128), generator=g, device=cuda_device).to(torch.bfloat16)
+    v = torch.randn((1, N, hkv, 128), generator=g, device=cuda_device).to(torch.bfloat16)
+    wt = atflash.WindowTable(128, 1e7, 2.0)
+    out = atflash.flash_attn_func(q, k, v, causal=True, window_table=wt)
+    torch.cuda.synchronize()
+    assert atflash.check_device_errors() == 0
+    w = OWT.wavelengths_sorted(128, 1e7, 2.0)
+    for t in (2047, 4095):
+        hi = (t + 1) * 128
+        for h in (5, 26):
+            hk = h // 7
+            qn = q[:, t * 128:hi, h:h + 1].transpose(1, 2).float().cpu().numpy()
+            kn = k[:, :hi, hk:hk + 1].transpose(1, 2).float().cpu().numpy()
+            vn = v[:, :hi, hk:hk + 1].transpose(1, 2).float().cpu().numpy()
+            ref = OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=BM, block_n=BN,
+                                     q_offset=t * 128)
+            got = out[:, t * 128:hi, h:h + 1].transpose(1, 2).float().cpu().numpy()
+            mx, mean = err_stats(got, ref)
+            assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (t, h, mx, mean)
