@@ -202,6 +202,42 @@ def cpu_baseline_sample(n_tiles=20, heads=7, k_ret=K_RET):
                                f"({flops:.3g} of {total:.3g}); {sec:.2f} s of CPU work"}
 
 
+def config1_cpu(k_rets=(2.0, float("inf"))):
+    """BASELINE config 1 on the host: the numpy oracle (ref_window_attn, fp32) at
+    batch 1, 24/8 heads, N=2048, theta 5e5, window k=2 and off, at the kernel's
+    tiling; ms per call (median of 3, all host threads)."""
+    import numpy as np
+    from oracle import attention as OA
+    from oracle import window_table as OWT
+    rng = np.random.default_rng(1)
+    f = lambda *sh: OA.bf16_round(rng.standard_normal(sh).astype(np.float32))
+    q, k, v = f(1, 24, 2048, 128), f(1, 8, 2048, 128), f(1, 8, 2048, 128)
+    res = {}
+    for kr in k_rets:
+        w = OWT.wavelengths_sorted(128, 5e5, kr)
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            OA.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128)
+            ts.append((time.perf_counter() - t0) * 1e3)
+        res["on_k2" if kr == 2.0 else "off"] = statistics.median(ts)
+    return res
+
+
+def config1_gpu(device):
+    """BASELINE config 1 on the GPU (prefill N=2048, 24/8 heads, k=2 and off): ms per call."""
+    import atflash
+    g = torch.Generator(device=device).manual_seed(11)
+    q = torch.randn((1, 2048, 24, D), generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn((1, 2048, 8, D), generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn((1, 2048, 8, D), generator=g, device=device).to(torch.bfloat16)
+    res = {}
+    for name, wt in (("on_k2", atflash.WindowTable(D, 5e5, 2.0)), ("off", None)):
+        ms, _ = timed(lambda i: atflash.prefill_fwd(q, k, v, causal=True, window_table=wt), 50, 5, 1)
+        res[name] = ms
+    return res
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -218,7 +254,8 @@ def run_reference(args, rank, world):
             "config": {"workload": "prefill N=131072 Hq=28 Hkv=4 d=128 theta=1e7 k=2 (BASELINE config 2)",
                        "batch": 1, "seq_len": N_CTX},
             "cpu_baseline": dict(info, value=v, unit="ms"),
-            "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config1_cpu_ms": config1_cpu()}
     print(json.dumps(line), flush=True)
 
 
@@ -438,9 +475,13 @@ def main():
         decode_1m = bench_decode_1m(device, rank, world, 20, 5, peaks)
         prefill_512k = bench_prefill_512k(device, rank, world, 2, 3, peaks)
     cpu = None
+    config1 = None
     if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
         cms, info = cpu_baseline_sample()
         cpu = dict(info, value=cms, unit="ms")
+        config1 = {"gpu_ms": config1_gpu(device), "cpu_oracle_ms": config1_cpu(),
+                   "cpu_cores": os.cpu_count(),
+                   "shape": "prefill batch 1, 24/8 heads, N=2048, d=128, theta 5e5 (BASELINE config 1)"}
     if rank == 0:
         achieved = my_flops / (ms_on * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -459,7 +500,8 @@ def main():
                            "l2": "inputs 1.2 GB per copy > 126 MB L2; two copies rotated"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
-                "device_error_flag": err, "extras": dict(extras, decode=decode, decode_1m_sharded=decode_1m, prefill_512k=prefill_512k)
+                "device_error_flag": err, "extras": dict(extras, decode=decode, decode_1m_sharded=decode_1m, prefill_512k=prefill_512k,
+                                config1=config1)
                 if extras else None}
         print(json.dumps(line), flush=True)
     if world > 1:
