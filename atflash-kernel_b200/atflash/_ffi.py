@@ -65,7 +65,9 @@ class AtfDecodeParams(ctypes.Structure):
                 ("zhi16", _i32 * 8), ("zhi8", _i32 * 16),
                 ("partial_o", _vp), ("partial_lse", _vp), ("out", _vp),
                 ("o_stride_b", _i64), ("o_stride_h", _i64), ("out_dtype", ctypes.c_int),
-                ("lse_out", _vp), ("error_flag", _vp)]
+                ("lse_out", _vp), ("error_flag", _vp),
+                ("k_level_major", ctypes.c_int), ("k_stride_page", _i64), ("k_stride_head", _i64),
+                ("k_stride_level", _i64)]
 
 
 class AtfMergeParams(ctypes.Structure):
@@ -90,7 +92,8 @@ class AtfAppendParams(ctypes.Structure):
                 ("kv_stride_head", _i64), ("num_kv_heads", _i32), ("head_dim", _i32), ("page_size", _i32),
                 ("batch_size", _i32), ("kv_indptr", _vp), ("kv_indices", _vp), ("cos", _vp), ("sin", _vp),
                 ("cs_stride_pos", _i64), ("n_pos", _i64), ("rope_positions", _vp), ("out_layout", ctypes.c_int),
-                ("error_flag", _vp)]
+                ("error_flag", _vp), ("k_level_major", ctypes.c_int), ("k_stride_page", _i64),
+                ("k_stride_head", _i64), ("k_stride_level", _i64)]
 
 
 class AtfError(RuntimeError):

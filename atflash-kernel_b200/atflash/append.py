@@ -47,20 +47,28 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, 
     else:
         kc, vc = paged_kv_cache[:, 0], paged_kv_cache[:, 1]
     dev = _runtime.require_cuda(append_key, append_value, kc, vc)
-    for t in (append_key, append_value, kc, vc):
+    k_level_major = kc.dim() == 5
+    for t in (append_key, append_value, vc) + (() if k_level_major else (kc,)):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.shape[-1] != 128:
             raise ValueError("keys, values and cache pages must be bf16 with a contiguous head_dim of 128")
     if append_key.shape != append_value.shape or append_key.stride() != append_value.stride():
         raise ValueError("append_key and append_value must have the same shape and strides")
-    if kc.shape != vc.shape or kc.stride() != vc.stride() or kc.dim() != 4:
+    if k_level_major:
+        # (P, Hkv, 8 levels, page, 16) sorted-pair K pages (see BatchDecodeWithPagedKVCacheWrapper.run)
+        if (kc.dtype != torch.bfloat16 or kc.shape[2] != 8 or kc.shape[4] != 16 or kc.stride(4) != 1
+                or kc.stride(3) != 16 or vc.dim() != 4 or kc.shape[0] != vc.shape[0]):
+            raise ValueError("level-major k pages must be (P, Hkv, 8, page, 16) bf16 with 16-element rows")
+        if rope is not None and out_layout != "sorted_pair":
+            raise ValueError("level-major k pages hold sorted-pair K")
+    elif kc.shape != vc.shape or kc.stride() != vc.stride() or kc.dim() != 4:
         raise ValueError("k and v pages must have the same 4-d shape and strides")
     nnz, hkv, _ = append_key.shape
     if kv_layout == "NHD":
-        npages, page, hk2, _ = kc.shape
-        s_page, s_tok, s_head = kc.stride(0), kc.stride(1), kc.stride(2)
+        npages, page, hk2, _ = vc.shape
+        s_page, s_tok, s_head = vc.stride(0), vc.stride(1), vc.stride(2)
     elif kv_layout == "HND":
-        npages, hk2, page, _ = kc.shape
-        s_page, s_head, s_tok = kc.stride(0), kc.stride(1), kc.stride(2)
+        npages, hk2, page, _ = vc.shape
+        s_page, s_head, s_tok = vc.stride(0), vc.stride(1), vc.stride(2)
     else:
         raise ValueError("kv_layout must be NHD or HND")
     if hk2 != hkv:
@@ -91,6 +99,11 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, 
             p.rope_positions = rp.data_ptr()
     p.out_layout = _LAYOUTS[out_layout]
     p.error_flag = _runtime.error_flag(dev).data_ptr()
+    if k_level_major:
+        if kc.shape[1] != hkv or kc.shape[3] != page:
+            raise ValueError("level-major k pages do not match the v pages")
+        p.k_level_major = 1
+        p.k_stride_page, p.k_stride_head, p.k_stride_level = kc.stride(0), kc.stride(1), kc.stride(2)
     with torch.cuda.device(dev):
         rc = _ffi.load().atf_paged_kv_append(ctypes.byref(p), _runtime.stream_handle(dev))
     _ffi.check("atf_paged_kv_append", rc)

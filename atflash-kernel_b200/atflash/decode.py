@@ -165,16 +165,26 @@ class BatchDecodeWithPagedKVCacheWrapper:
         dev = _runtime.require_cuda(q, kc, vc)
         if kc.dtype != torch.bfloat16 or vc.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
             raise TypeError("q and the KV cache must be bfloat16")
-        if kc.stride() != vc.stride() or kc.shape != vc.shape or kc.dim() != 4:
+        # K pages are either laid out like V (4-d, NHD / HND) or level-major:
+        # (P, Hkv, 8 levels, page, 16) in sorted-pair order, so that a page's
+        # in-window levels are one contiguous run
+        k_level_major = kc.dim() == 5
+        if k_level_major:
+            if (kc.shape[2] != 8 or kc.shape[4] != 16 or kc.stride(4) != 1 or kc.stride(3) != 16
+                    or vc.dim() != 4 or kc.shape[0] != vc.shape[0]):
+                raise ValueError("level-major k pages must be (P, Hkv, 8, page, 16) with 16-element rows")
+        elif kc.stride() != vc.stride() or kc.shape != vc.shape or kc.dim() != 4:
             raise ValueError("k and v pages must have the same 4-d shape and strides")
-        if kc.stride(-1) != 1 or q.stride(-1) != 1:
+        if vc.stride(-1) != 1 or q.stride(-1) != 1:
             raise ValueError("the head_dim axis must be contiguous")
         if self._kv_layout == "NHD":
-            _, page, hkv, d = kc.shape
-            s_page, s_tok, s_head = kc.stride(0), kc.stride(1), kc.stride(2)
+            _, page, hkv, d = vc.shape
+            s_page, s_tok, s_head = vc.stride(0), vc.stride(1), vc.stride(2)
         else:
-            _, hkv, page, d = kc.shape
-            s_page, s_head, s_tok = kc.stride(0), kc.stride(1), kc.stride(2)
+            _, hkv, page, d = vc.shape
+            s_page, s_head, s_tok = vc.stride(0), vc.stride(1), vc.stride(2)
+        if k_level_major and (kc.shape[1] != hkv or kc.shape[3] != page):
+            raise ValueError("level-major k pages do not match the v pages")
         if page != P["page_size"] or hkv != P["Hkv"] or d != 128:
             raise ValueError("KV cache shape does not match the plan")
         B, Hq = P["B"], P["Hq"]
@@ -220,6 +230,9 @@ class BatchDecodeWithPagedKVCacheWrapper:
         a.out_dtype = _ffi.ATF_DTYPE_F32 if out.dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
         a.lse_out = lse.data_ptr() if lse is not None else None
         a.error_flag = _runtime.error_flag(dev).data_ptr()
+        if k_level_major:
+            a.k_level_major = 1
+            a.k_stride_page, a.k_stride_head, a.k_stride_level = kc.stride(0), kc.stride(1), kc.stride(2)
         with torch.cuda.device(dev):
             rc = _ffi.load().atf_decode_run(ctypes.byref(a), _runtime.stream_handle(dev))
         _ffi.check("atf_decode_run", rc)

@@ -33,6 +33,8 @@ struct Args {
   const int64_t* rope_pos;
   int rope, sorted;
   int* err;
+  int k_lm;                              // level-major K pages
+  long long k_s_page, k_s_head, k_s_level;
 };
 
 __global__ void append_kernel(const Args a) {
@@ -58,22 +60,29 @@ __global__ void append_kernel(const Args a) {
     if (a.err != nullptr && c == 0) atomicCAS(a.err, 0, kDevErrIndex);
     return;
   }
-  const long long dst = page * a.s_page + static_cast<long long>(pos % a.page_size) * a.s_tok +
-                        static_cast<long long>(h) * a.s_head;
+  const long long slot = pos % a.page_size;
+  const long long dst = page * a.s_page + slot * a.s_tok + static_cast<long long>(h) * a.s_head;
   const long long src = i * a.as_n + static_cast<long long>(h) * a.as_h;
   // V: plain copy of dims [8c, 8c+8) and [64+8c, 64+8c+8)
   *reinterpret_cast<uint4*>(a.vc + dst + 8 * c) = *reinterpret_cast<const uint4*>(a.av + src + 8 * c);
   *reinterpret_cast<uint4*>(a.vc + dst + 64 + 8 * c) = *reinterpret_cast<const uint4*>(a.av + src + 64 + 8 * c);
+  // K row base and level stride: a plain row has its 16-dim levels 16 apart;
+  // level-major pages keep each level of the page as its own run of 16-dim rows
+  const long long kdst = a.k_lm ? page * a.k_s_page + static_cast<long long>(h) * a.k_s_head + slot * 16 : dst;
+  const long long lstride = a.k_lm ? a.k_s_level : 16;
   if (!a.rope) {
-    *reinterpret_cast<uint4*>(a.kc + dst + 8 * c) = *reinterpret_cast<const uint4*>(a.ak + src + 8 * c);
-    *reinterpret_cast<uint4*>(a.kc + dst + 64 + 8 * c) = *reinterpret_cast<const uint4*>(a.ak + src + 64 + 8 * c);
+    // dims [8c, 8c+8) are half (c & 1) of level c/2, dims [64+8c, ..) of level 4 + c/2
+    *reinterpret_cast<uint4*>(a.kc + kdst + (c >> 1) * lstride + 8 * (c & 1)) =
+        *reinterpret_cast<const uint4*>(a.ak + src + 8 * c);
+    *reinterpret_cast<uint4*>(a.kc + kdst + (4 + (c >> 1)) * lstride + 8 * (c & 1)) =
+        *reinterpret_cast<const uint4*>(a.ak + src + 64 + 8 * c);
     return;
   }
   long long rp = a.rope_pos != nullptr ? a.rope_pos[i] : pos;
   if (rp < 0) rp = 0;
   if (rp >= a.n_pos) rp = a.n_pos - 1;
-  ropemath::rotate_chunk(a.ak + src, a.cs + rp * a.cs_stride, a.sn + rp * a.cs_stride, a.kc + dst, c,
-                         a.sorted != 0);
+  ropemath::rotate_chunk(a.ak + src, a.cs + rp * a.cs_stride, a.sn + rp * a.cs_stride, a.kc + kdst, c,
+                         a.sorted != 0, lstride);
 }
 
 }  // namespace append
@@ -94,6 +103,12 @@ extern "C" int atf_paged_kv_append(const AtfAppendParams* p, atf_stream_t stream
   if (rope && (p->n_pos < 1 || p->cs_stride_pos < 64)) return ATF_ERR_INVALID_ARG;
   if (p->out_layout != ATF_LAYOUT_SORTED_PAIR && p->out_layout != ATF_LAYOUT_ROTATE_HALF)
     return ATF_ERR_INVALID_ARG;
+  if (p->k_level_major) {
+    if (rope && p->out_layout != ATF_LAYOUT_SORTED_PAIR) return ATF_ERR_UNSUPPORTED;
+    if ((p->k_stride_page & 7) || (p->k_stride_head & 7) || (p->k_stride_level & 7) ||
+        p->k_stride_level < 16 * static_cast<int64_t>(p->page_size))
+      return ATF_ERR_ALIGNMENT;
+  }
   if (!aligned16(p->append_k) || !aligned16(p->append_v) || !aligned16(p->k_cache) ||
       !aligned16(p->v_cache) || (p->a_stride_n & 7) || (p->a_stride_h & 7) || (p->kv_stride_page & 7) ||
       (p->kv_stride_token & 7) || (p->kv_stride_head & 7))
@@ -130,6 +145,10 @@ extern "C" int atf_paged_kv_append(const AtfAppendParams* p, atf_stream_t stream
   a.rope = rope ? 1 : 0;
   a.sorted = p->out_layout == ATF_LAYOUT_SORTED_PAIR ? 1 : 0;
   a.err = p->error_flag;
+  a.k_lm = p->k_level_major ? 1 : 0;
+  a.k_s_page = p->k_stride_page;
+  a.k_s_head = p->k_stride_head;
+  a.k_s_level = p->k_stride_level;
   const int threads = 256;
   const long long blocks = (total + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;

@@ -936,6 +936,13 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   const bool tma_path = (ps == 16 || ps == 32 || ps == 64 || ps == 128 || ps == 256) &&
                         p->qk_layout == ATF_LAYOUT_SORTED_PAIR && p->window != ATF_WINDOW_VEC8 &&
                         p->num_pages >= 1;
+  if (p->k_level_major) {
+    // only the TMA kernel reads level-major K pages
+    if (!tma_path) return ATF_ERR_UNSUPPORTED;
+    if ((p->k_stride_page & 7) || (p->k_stride_head & 7) || (p->k_stride_level & 7) ||
+        p->k_stride_level < 16 * static_cast<int64_t>(ps))
+      return ATF_ERR_ALIGNMENT;
+  }
   if (p->num_items > 0) {
     decode::Args a;
     a.q = static_cast<const __nv_bfloat16*>(p->q);
@@ -975,9 +982,15 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
       const uint64_t hkv = static_cast<uint64_t>(p->num_kv_heads), npg = static_cast<uint64_t>(p->num_pages);
       const uint64_t kdims[5] = {16, static_cast<uint64_t>(ps), ATF_MAX_LEVELS, hkv, npg};
       const uint64_t vdims[5] = {64, static_cast<uint64_t>(ps), 2, hkv, npg};
-      const uint64_t kstr[4] = {stride_b(ps, p->kv_stride_token), 32, stride_b(hkv, p->kv_stride_head),
+      const uint64_t vstr[4] = {stride_b(ps, p->kv_stride_token), 128, stride_b(hkv, p->kv_stride_head),
                                 stride_b(npg, p->kv_stride_page)};
-      const uint64_t vstr[4] = {kstr[0], 128, kstr[2], kstr[3]};
+      // K: the same view as V for NHD / HND pages (level stride 32 B inside a
+      // row); level-major pages have 32-byte token rows and a level stride of
+      // at least a page of rows, so a slice's L levels are one contiguous run
+      const uint64_t kstr[4] = {p->k_level_major ? 32ull : vstr[0],
+                                p->k_level_major ? static_cast<uint64_t>(p->k_stride_level) * 2ull : 32ull,
+                                p->k_level_major ? stride_b(hkv, p->k_stride_head) : vstr[2],
+                                p->k_level_major ? stride_b(npg, p->k_stride_page) : vstr[3]};
       const uint32_t rows = static_cast<uint32_t>(ps < 64 ? ps : 64);
       decode_tma::KMaps tk;
       CUtensorMap tv;
@@ -985,8 +998,10 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
       // of each 256-byte row) are not fetched from HBM along with its prefix
       for (int L = 1; L <= ATF_MAX_LEVELS; ++L) {
         const uint32_t kbox[5] = {16, rows, static_cast<uint32_t>(L), 1, 1};
+        // (level-major pages: every fetched byte is used, so full promotion)
         if ((rc = encode_tiled_bf16(&tk.lv[L - 1], p->k_cache, 5, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_32B,
-                                    CU_TENSOR_MAP_L2_PROMOTION_NONE)) != ATF_OK)
+                                    p->k_level_major ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                                     : CU_TENSOR_MAP_L2_PROMOTION_NONE)) != ATF_OK)
           return rc;
       }
       const uint32_t vbox[5] = {64, rows, 2, 1, 1};

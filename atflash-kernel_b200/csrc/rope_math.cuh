@@ -24,9 +24,11 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
 // Rotates HF pairs r = 8c..8c+7 of one row: xr points at the row (HF order),
 // cr / sr at the position's cos / sin table rows. Writes the rotated chunk to
 // orow in rotate_half order (dims [8c, 8c+8) and [64+8c, 64+8c+8)) or, when
-// sorted, to the 32 contiguous bytes of sorted pairs 8(7-c)..8(7-c)+7.
+// sorted, to the 32 contiguous bytes of sorted pairs 8(7-c)..8(7-c)+7, i.e.
+// 16-dim level 7-c at orow + level * level_stride (16 for a plain row).
 __device__ __forceinline__ void rotate_chunk(const __nv_bfloat16* xr, const float* cr, const float* sr,
-                                             __nv_bfloat16* orow, int c, bool sorted) {
+                                             __nv_bfloat16* orow, int c, bool sorted,
+                                             long long level_stride = 16) {
   const uint4 lo = *reinterpret_cast<const uint4*>(xr + 8 * c);
   const uint4 hi = *reinterpret_cast<const uint4*>(xr + 64 + 8 * c);
   const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
@@ -51,7 +53,7 @@ __device__ __forceinline__ void rotate_chunk(const __nv_bfloat16* xr, const floa
     uint32_t w[8];
 #pragma unroll
     for (int jl = 0; jl < 8; ++jl) w[jl] = pack_rn(r1[7 - jl], r2[7 - jl]);
-    uint4* dst = reinterpret_cast<uint4*>(orow + 16 * (7 - c));
+    uint4* dst = reinterpret_cast<uint4*>(orow + level_stride * (7 - c));
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }

@@ -275,18 +275,25 @@ def bench_decode(device, steps, warmup, peaks, N=131072):
     indptr = torch.arange(0, total + 1, npg, dtype=torch.int32)
     lpl = torch.full((B,), page, dtype=torch.int32)
     ws = torch.empty(128 * 1024 * 1024, dtype=torch.uint8, device=device)
+    # the same K pages laid out level-major (P, Hkv, 8, page, 16): a page's
+    # in-window levels are one contiguous run
+    kc_lm = kc.view(total, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous()
     res = {}
-    for name, wt in (("on", atflash.WindowTable(D, 5e5, 2.0)), ("off", None)):
+    for name, wt, kk in (("on", atflash.WindowTable(D, 5e5, 2.0), kc), ("off", None, kc),
+                         ("on_level_major_k", atflash.WindowTable(D, 5e5, 2.0), kc_lm),
+                         ("off_level_major_k", None, kc_lm)):
         w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
         w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt)
         out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=device)
-        ms, _ = timed(lambda i: w.run(q, (kc, vc), out=out), steps, warmup, 1)
+        ms, _ = timed(lambda i: w.run(q, (kk, vc), out=out), steps, warmup, 1)
         zhi = wt.zhi16 if wt is not None else None
         byts = WT.decode_bytes(hkv, [N] * B, zhi)["bytes"]
         res[name] = {"us": ms * 1e3, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9}
     res["ratio_on_off"] = res["off"]["us"] / res["on"]["us"]
     res["hbm_frac_on"] = res["on"]["gbs"] / peaks["hbm_gbs"]
-    del kc, vc
+    res["ratio_on_off_level_major_k"] = res["off_level_major_k"]["us"] / res["on_level_major_k"]["us"]
+    res["hbm_frac_on_level_major_k"] = res["on_level_major_k"]["gbs"] / peaks["hbm_gbs"]
+    del kc, vc, kc_lm
     torch.cuda.empty_cache()
     return res
 

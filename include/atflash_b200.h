@@ -172,6 +172,12 @@ typedef struct {
   int out_dtype;      /* ATF_DTYPE_BF16 or ATF_DTYPE_F32 */
   float* lse_out;     /* optional fp32 [B, Hq], natural log */
   int* error_flag;
+  /* Level-major K pages (optional, 0 = k_cache uses the kv strides above):
+   * k_cache is [P, Hkv, 8 levels, page, 16] bf16 in sorted-pair order, so the
+   * in-window levels of a page are one contiguous run. Needs the sorted-pair
+   * layout, the 16-snap or no window and a page size of 16..256 (power of 2). */
+  int k_level_major;
+  int64_t k_stride_page, k_stride_head, k_stride_level; /* elements; the token stride is 16 */
 } AtfDecodeParams;
 
 /* Paged-KV GQA split-KV decode followed by the LSE merge of its splits. */
@@ -268,6 +274,10 @@ typedef struct {
   const int64_t* rope_positions;  /* optional device [nnz]: RoPE position (default: positions[i]) */
   int out_layout;                 /* with RoPE: pair order written (ATF_LAYOUT_*) */
   int* error_flag;                /* optional: set to 2 when a token's page index is out of range */
+  /* Level-major K pages (see AtfDecodeParams): K is written as [P, Hkv, 8, page, 16]
+   * in sorted-pair order (with RoPE, out_layout must be sorted pair). */
+  int k_level_major;
+  int64_t k_stride_page, k_stride_head, k_stride_level;
 } AtfAppendParams;
 
 /* Append K/V tokens to a paged cache: token i goes to page

@@ -130,3 +130,31 @@ def test_decode_over_appended_cache():
     torch.cuda.synchronize()
     assert atflash.check_device_errors() == 0
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("rope", [False, True])
+def test_append_into_level_major_k_pages(rope):
+    """Appending into level-major K pages writes the same values as appending
+    into NHD pages and laying them out level-major."""
+    import atflash
+    dev = torch.device("cuda:0")
+    g, kc, vc, indptr, indices, lens = _setup("NHD", 15)
+    nnz = sum(lens)
+    bidx, pos = atflash.get_batch_indices_positions(torch.tensor([0, 37, 117, 122]), torch.tensor(lens), nnz)
+    k = torch.randn((nnz, 4, 128), generator=g).to(torch.bfloat16)
+    v = torch.randn((nnz, 4, 128), generator=g).to(torch.bfloat16)
+    kw = {}
+    if rope:
+        cos, sin = rope_tables(200, 128, 1e4)
+        kw = dict(rope=(cos.to(dev), sin.to(dev)), out_layout="sorted_pair")
+    P, page, hkv, _ = kc.shape
+    k_nhd, v_nhd = kc.to(dev), vc.to(dev)
+    k_lm = kc.view(P, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous().to(dev)
+    v_lm = vc.to(dev)
+    args = (k.to(dev), v.to(dev), bidx.to(dev), pos.to(dev))
+    atflash.append_paged_kv_cache(*args, (k_nhd, v_nhd), indices.to(dev), indptr.to(dev), **kw)
+    atflash.append_paged_kv_cache(*args, (k_lm, v_lm), indices.to(dev), indptr.to(dev), **kw)
+    torch.cuda.synchronize()
+    assert atflash.check_device_errors() == 0
+    expect = k_nhd.view(P, page, hkv, 8, 16).permute(0, 2, 3, 1, 4)
+    assert torch.equal(k_lm, expect) and torch.equal(v_lm, v_nhd)

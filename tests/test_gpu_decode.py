@@ -255,3 +255,22 @@ def test_prefill_with_rope_end_to_end(cuda_device):
                              block_m=128, block_n=128)
     mx, mean = err_stats(out.transpose(1, 2).float().cpu().numpy(), ref)
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+
+
+def _level_major(kc):
+    """(P, page, Hkv, 128) NHD sorted-pair K pages -> level-major (P, Hkv, 8, page, 16)."""
+    P, page, hkv, _ = kc.shape
+    return kc.view(P, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous()
+
+
+@pytest.mark.parametrize("page,k_ret", [(16, 2.0), (64, 2.0), (16, None), (128, 1.0)])
+def test_decode_level_major_k_pages_equal_nhd(cuda_device, page, k_ret):
+    """Level-major K pages (a page's in-window levels contiguous) give the same
+    decode as the NHD pages they were laid out from, bit for bit."""
+    import atflash
+    lens, hq, hkv = [3000, 517, 64], 24, 8
+    q, kc, vc, indptr, indices, lpl, _, _ = make_paged(lens, hq, hkv, page, 40 + page)
+    wt = atflash.WindowTable(128, 1e4, k_ret) if k_ret is not None else None
+    ref = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, window_table=wt)
+    got = run_decode(cuda_device, q, _level_major(kc), vc, indptr, indices, lpl, hq, hkv, page, window_table=wt)
+    assert torch.equal(ref, got)
