@@ -1,11 +1,11 @@
 #!/usr/bin/env python
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container where the reference tree is mounted (its path is given by
---reference, default /root/reference); the fixtures are committed so that the
-tests never need the reference at run time:
+Run where the reference tree is available (its path is given by --reference or
+the ATFLASH_REFERENCE environment variable); the fixtures are committed so that
+the tests never need the reference at run time:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference tree>
 
 What is recorded, all produced by the reference's own code:
   w_meta_tables.json  the reference's recorded RoPE-scaled window inputs
@@ -83,8 +83,10 @@ def build_inputs(G2, hq, hkv, N, d, base, seed, phase):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ATFLASH_REFERENCE"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference tree with --reference or ATFLASH_REFERENCE")
     ref = args.reference
     sys.path[:0] = [os.path.join(ref, "window_tables"),
                     os.path.join(ref, "kernels", "flashinfer_port"), ref,
