@@ -86,6 +86,9 @@ CASES = [
     ([1500, 64, 1], 28, 4, 64, "HND", 1e4, 1.0),
     ([4096, 100], 8, 8, 16, "HND", 1e4, 3.0),
     ([5000], 16, 1, 16, "NHD", 1e4, 2.0),
+    ([700, 1200], 4, 2, 16, "NHD", 1e4, 2.0),       # GQA group 2
+    ([2500], 16, 4, 64, "NHD", 5e5, 2.0),           # GQA group 4
+    ([1800, 33], 32, 4, 16, "HND", 1e4, 2.0),       # GQA group 8
 ]
 
 

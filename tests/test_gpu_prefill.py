@@ -61,6 +61,9 @@ CASES = [
     (24, 8, 2048, 5e5, 2.0, 777),
     (28, 4, 1536, 1e7, 2.0, 11),
     (14, 2, 1000, 1e4, 3.0, 12),
+    (4, 2, 384, 1e4, 2.0, 13),     # GQA group 2
+    (8, 2, 640, 1e4, 2.0, 14),     # GQA group 4
+    (8, 1, 512, 5e5, 2.0, 15),     # GQA group 8
 ]
 
 
@@ -77,6 +80,19 @@ def test_prefill_parity(cuda_device, case, window):
     anchor = float(np.abs(ref16 - ref32).max())
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
     assert mx <= 2 * anchor + 2e-3, (mx, anchor)
+
+
+def test_prefill_batch_of_two(cuda_device):
+    """Two sequences in one call (B = 2, GQA group 4): each batch row matches the
+    oracle run on its own."""
+    hq, hkv, N, base, k_ret = 8, 2, 384, 1e4, 2.0
+    parts = [make_bhsd(hq, hkv, N, 128, base, seed) for seed in (21, 22)]
+    q, k, v = (torch.cat([p[i] for p in parts], dim=0) for i in range(3))
+    out = _run(q, k, v, cuda_device, base, k_ret).transpose(1, 2).float().cpu().numpy()
+    for b, (qb, kb, vb, _) in enumerate(parts):
+        ref32 = _oracle(qb, kb, vb, base, k_ret)
+        mx, mean = err_stats(out[b:b + 1], ref32)
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (b, mx, mean)
 
 
 @pytest.mark.parametrize("case", [(3, 1, 448, 1e4, 2.0, 777), (7, 1, 320, 1e4, 1.0, 778)],
