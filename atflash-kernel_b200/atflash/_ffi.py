@@ -22,7 +22,7 @@ ATF_NOALLOC_MAX_PARTIAL_ROWS = 16384
 EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_window_deff",
             "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
             "atf_rope_pack", "atf_paged_kv_append", "atf_status_string", "atf_version",
-            "atf_read_error_flag", "atf_selftest_wait_timeout")
+            "atf_read_error_flag", "atf_selftest_wait_timeout", "atf_params_size")
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
 
@@ -74,7 +74,7 @@ class AtfMergeParams(ctypes.Structure):
     _fields_ = [("part_o", _vp), ("part_lse", _vp), ("part_indptr", _vp), ("num_parts", _i32),
                 ("batch", _i32), ("num_heads", _i32), ("head_dim", _i32), ("lse_log2", ctypes.c_int),
                 ("out", _vp), ("o_stride_b", _i64), ("o_stride_h", _i64), ("out_dtype", ctypes.c_int),
-                ("lse_out", _vp)]
+                ("lse_out", _vp), ("part_stride_o", _i64), ("part_stride_lse", _i64)]
 
 
 class AtfRopeParams(ctypes.Structure):
@@ -135,9 +135,11 @@ def load() -> ctypes.CDLL:
             lib.atf_status_string.restype = ctypes.c_char_p
             lib.atf_read_error_flag.argtypes = [_vp, P(ctypes.c_int)]
             lib.atf_selftest_wait_timeout.argtypes = [_vp, _vp]
+            lib.atf_params_size.argtypes = [ctypes.c_char_p]
             for name in EXPORTED:
-                if name not in ("atf_status_string",):
+                if name not in ("atf_status_string", "atf_params_size"):
                     getattr(lib, name).restype = ctypes.c_int
+            lib.atf_params_size.restype = _i64
             _lib = lib
     return _lib
 

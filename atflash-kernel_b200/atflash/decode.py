@@ -243,13 +243,29 @@ class BatchDecodeWithPagedKVCacheWrapper:
 
 def lse_merge(part_o: torch.Tensor, part_lse: torch.Tensor, *, lse_log2: bool = False,
               out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False):
-    """Merge P partial states: part_o (P, B, H, 128) fp32, part_lse (P, B, H) fp32."""
+    """Merge P partial states: part_o (P, B, H, 128) fp32, part_lse (P, B, H) fp32.
+    The parts may be strided views (e.g. of one all-gathered flat buffer): each
+    part's own block must be contiguous, the part stride of part_o a multiple of 4."""
     dev = _runtime.require_cuda(part_o, part_lse)
     Pn, B, H, D = part_o.shape
     if D != 128 or tuple(part_lse.shape) != (Pn, B, H):
         raise ValueError("part_o must be (P, B, H, 128) and part_lse (P, B, H)")
-    part_o = part_o.float().contiguous()
-    part_lse = part_lse.float().contiguous()
+    part_o = part_o.float()
+    part_lse = part_lse.float()
+
+    def _parts_ok(t, align0):
+        # each part's block contiguous; the part stride spans at least a block
+        exp = 1
+        for dim in range(t.dim() - 1, 0, -1):
+            if t.shape[dim] != 1 and t.stride(dim) != exp:
+                return False
+            exp *= t.shape[dim]
+        return t.shape[0] == 1 or (t.stride(0) >= exp and t.stride(0) % align0 == 0)
+
+    if not _parts_ok(part_o, 4):
+        part_o = part_o.contiguous()
+    if not _parts_ok(part_lse, 1):
+        part_lse = part_lse.contiguous()
     out = torch.empty((B, H, D), dtype=out_dtype, device=dev)
     lse = torch.empty((B, H), dtype=torch.float32, device=dev) if return_lse else None
     m = _ffi.AtfMergeParams()
@@ -259,6 +275,8 @@ def lse_merge(part_o: torch.Tensor, part_lse: torch.Tensor, *, lse_log2: bool = 
     m.out, m.o_stride_b, m.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
     m.out_dtype = _ffi.ATF_DTYPE_F32 if out_dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
     m.lse_out = lse.data_ptr() if lse is not None else None
+    m.part_stride_o = part_o.stride(0) if Pn > 1 else 0
+    m.part_stride_lse = part_lse.stride(0) if Pn > 1 else 0
     with torch.cuda.device(dev):
         rc = _ffi.load().atf_lse_merge(ctypes.byref(m), _runtime.stream_handle(dev))
     _ffi.check("atf_lse_merge", rc)

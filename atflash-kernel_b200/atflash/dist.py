@@ -109,24 +109,42 @@ def gather_zigzag(outs, seqlen: int, world: int, group=None) -> torch.Tensor:
     return full
 
 
+def _gather_and_merge(pack, B, H, D, group, world, merge_fn, out_dtype):
+    """All-gather one flat fp32 buffer per rank ([B*H*D] O, then [B*H] LSE, padded to
+    a multiple of 4 floats) and merge the ranks' states in place."""
+    n = pack.numel()
+    allp = pack.new_empty((world * n,))
+    dist.all_gather_into_tensor(allp, pack, group=group)
+    po = allp.as_strided((world, B, H, D), (n, H * D, D, 1))
+    pl = allp.as_strided((world, B, H), (n, H, 1), B * H * D)
+    if merge_fn is None:
+        from .decode import lse_merge
+        return lse_merge(po, pl, lse_log2=False, out_dtype=out_dtype, return_lse=True)
+    return merge_fn(po, pl)
+
+
+def _pack_views(B, H, D, device):
+    n_o, n_l = B * H * D, (B * H + 3) // 4 * 4
+    pack = torch.empty((n_o + n_l,), dtype=torch.float32, device=device)
+    return pack, pack[:n_o].view(B, H, D), pack[n_o:n_o + B * H].view(B, H)
+
+
 def merge_partials(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
                    merge_fn: Optional[Callable] = None, out_dtype=torch.bfloat16):
     """All-gather per-rank partial states (O fp32 (B,H,D), LSE natural (B,H)) and
     merge them: LSE = log sum exp LSE_r, O = sum exp(LSE_r - LSE) O_r."""
     _, world = _rank_world(group)
     B, H, D = o_local.shape
-    pack = torch.cat([o_local.float().reshape(B * H, D), lse_local.float().reshape(B * H, 1)], dim=1)
-    allp = pack.new_empty((world,) + tuple(pack.shape))
-    if world > 1:
-        dist.all_gather_into_tensor(allp.view(-1), pack.contiguous().view(-1), group=group)
-    else:
-        allp[0] = pack
-    po = allp[:, :, :D].reshape(world, B, H, D)
-    pl = allp[:, :, D].reshape(world, B, H)
-    if merge_fn is None:
-        from .decode import lse_merge
-        return lse_merge(po, pl, lse_log2=False, out_dtype=out_dtype, return_lse=True)
-    return merge_fn(po, pl)
+    if world == 1:
+        po, pl = o_local.float()[None], lse_local.float()[None]
+        if merge_fn is None:
+            from .decode import lse_merge
+            return lse_merge(po, pl, lse_log2=False, out_dtype=out_dtype, return_lse=True)
+        return merge_fn(po, pl)
+    pack, o_view, l_view = _pack_views(B, H, D, o_local.device)
+    o_view.copy_(o_local)
+    l_view.copy_(lse_local)
+    return _gather_and_merge(pack, B, H, D, group, world, merge_fn, out_dtype)
 
 
 def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
@@ -139,6 +157,9 @@ def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Ten
         # one shard: the decode's own split merge is already the result
         return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
                            out_dtype=out_dtype)
-    o, lse = wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
-                         out_dtype=torch.float32)
-    return merge_partials(o, lse, group=group, out_dtype=out_dtype)
+    # the local state goes straight into the buffer that is all-gathered
+    B, H, D = q.shape
+    pack, o_view, l_view = _pack_views(B, H, D, q.device)
+    wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=o_view, lse=l_view, return_lse=True,
+                out_dtype=torch.float32)
+    return _gather_and_merge(pack, B, H, D, group, world, None, out_dtype)

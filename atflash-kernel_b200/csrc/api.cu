@@ -1,5 +1,6 @@
 // C-ABI glue: window tables, status strings, device checks, TMA descriptor
 // encoding through the driver entry point.
+#include <cstring>
 #include <math.h>
 
 #include <mutex>
@@ -64,6 +65,26 @@ int check_device(int* device_out) {
 using namespace atf;
 
 extern "C" int atf_version(void) { return 100; }
+
+extern "C" int64_t atf_params_size(const char* name) {
+  if (name == nullptr) return -1;
+  struct Entry {
+    const char* n;
+    int64_t size;
+  };
+  static const Entry kSizes[] = {
+      {"AtfPrefillParams", static_cast<int64_t>(sizeof(AtfPrefillParams))},
+      {"AtfDecodePlanParams", static_cast<int64_t>(sizeof(AtfDecodePlanParams))},
+      {"AtfDecodePlan", static_cast<int64_t>(sizeof(AtfDecodePlan))},
+      {"AtfDecodeParams", static_cast<int64_t>(sizeof(AtfDecodeParams))},
+      {"AtfMergeParams", static_cast<int64_t>(sizeof(AtfMergeParams))},
+      {"AtfRopeParams", static_cast<int64_t>(sizeof(AtfRopeParams))},
+      {"AtfAppendParams", static_cast<int64_t>(sizeof(AtfAppendParams))},
+  };
+  for (const Entry& e : kSizes)
+    if (std::strcmp(e.n, name) == 0) return e.size;
+  return -1;
+}
 
 extern "C" const char* atf_status_string(int s) {
   switch (s) {

@@ -719,6 +719,9 @@ struct Args {
   const float* pl;
   const int* indptr;
   int P, B, H;
+  // uniform parts: floats between consecutive parts of po / pl (0: packed
+  // [P, B, H, 128] / [P, B, H])
+  long long part_stride_o, part_stride_l;
   int lse_log2;
   void* out;
   long long o_sb, o_sh;
@@ -742,23 +745,27 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = bh / a.H, h = bh % a.H;
   int p0, p1;
-  long long stride_p;  // distance between consecutive parts of this (b, h), in rows of H
-  long long base;
+  // part i of this (b, h): O at po + ob + i * so, LSE at pl[lb + i * sl] (floats)
+  long long lb, sl, ob, so;
   if (a.indptr != nullptr) {
     p0 = a.indptr[b];
     p1 = a.indptr[b + 1];
-    base = static_cast<long long>(p0) * a.H + h;
-    stride_p = a.H;
+    lb = static_cast<long long>(p0) * a.H + h;
+    sl = a.H;
+    ob = lb * 128;
+    so = sl * 128;
   } else {
     p0 = 0;
     p1 = a.P;
-    base = static_cast<long long>(b) * a.H + h;
-    stride_p = static_cast<long long>(a.B) * a.H;
+    lb = static_cast<long long>(b) * a.H + h;
+    ob = lb * 128;
+    sl = a.part_stride_l > 0 ? a.part_stride_l : static_cast<long long>(a.B) * a.H;
+    so = a.part_stride_o > 0 ? a.part_stride_o : static_cast<long long>(a.B) * a.H * 128;
   }
   const int n = p1 - p0;
   const float cvt = a.lse_log2 ? 1.0f : 1.4426950408889634f;  // to log2
   float M = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += MERGE_WARPS * 32) M = fmaxf(M, a.pl[base + i * stride_p] * cvt);
+  for (int i = threadIdx.x; i < n; i += MERGE_WARPS * 32) M = fmaxf(M, a.pl[lb + i * sl] * cvt);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   if (lane == 0) s_red[warp] = M;
@@ -770,10 +777,9 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
   float L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   auto add = [&](int i) {
-    const long long r = base + i * stride_p;
-    const float lp = a.pl[r] * cvt;
+    const float lp = a.pl[lb + i * sl] * cvt;
     const float wgt = (lp == -INFINITY) ? 0.f : exp2f(lp - M);
-    const float4 v = *reinterpret_cast<const float4*>(a.po + r * 128 + lane * 4);
+    const float4 v = *reinterpret_cast<const float4*>(a.po + ob + i * so + lane * 4);
     L += wgt;
     acc.x += wgt * v.x;
     acc.y += wgt * v.y;
@@ -783,13 +789,15 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
   int i = warp;
   for (; i + 3 * MERGE_WARPS < n; i += 4 * MERGE_WARPS) {
     // four independent parts per iteration keep four loads in flight
-    const long long r0 = base + i * stride_p, r1 = r0 + MERGE_WARPS * stride_p;
-    const long long r2 = r1 + MERGE_WARPS * stride_p, r3 = r2 + MERGE_WARPS * stride_p;
-    const float l0 = a.pl[r0] * cvt, l1 = a.pl[r1] * cvt, l2 = a.pl[r2] * cvt, l3 = a.pl[r3] * cvt;
-    const float4 v0 = *reinterpret_cast<const float4*>(a.po + r0 * 128 + lane * 4);
-    const float4 v1 = *reinterpret_cast<const float4*>(a.po + r1 * 128 + lane * 4);
-    const float4 v2 = *reinterpret_cast<const float4*>(a.po + r2 * 128 + lane * 4);
-    const float4 v3 = *reinterpret_cast<const float4*>(a.po + r3 * 128 + lane * 4);
+    const long long q0 = lb + i * sl, dq = MERGE_WARPS * sl;
+    const float* o0 = a.po + ob + i * so + lane * 4;
+    const long long dso = MERGE_WARPS * so;
+    const float l0 = a.pl[q0] * cvt, l1 = a.pl[q0 + dq] * cvt, l2 = a.pl[q0 + 2 * dq] * cvt,
+                l3 = a.pl[q0 + 3 * dq] * cvt;
+    const float4 v0 = *reinterpret_cast<const float4*>(o0);
+    const float4 v1 = *reinterpret_cast<const float4*>(o0 + dso);
+    const float4 v2 = *reinterpret_cast<const float4*>(o0 + 2 * dso);
+    const float4 v3 = *reinterpret_cast<const float4*>(o0 + 3 * dso);
     const float w0 = (l0 == -INFINITY) ? 0.f : exp2f(l0 - M);
     const float w1 = (l1 == -INFINITY) ? 0.f : exp2f(l1 - M);
     const float w2 = (l2 == -INFINITY) ? 0.f : exp2f(l2 - M);
@@ -1024,6 +1032,8 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
     if (cudaGetLastError() != cudaSuccess) return ATF_ERR_CUDA;
   }
   merge::Args m;
+  m.part_stride_o = 0;
+  m.part_stride_l = 0;
   m.po = p->partial_o;
   m.pl = p->partial_lse;
   m.indptr = p->item_indptr;
@@ -1048,7 +1058,14 @@ extern "C" int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream) {
   if (!aligned16(p->part_o) || (p->out_dtype == ATF_DTYPE_F32 && !aligned16(p->out)) ||
       (reinterpret_cast<uintptr_t>(p->out) & 7) || (p->o_stride_b & 3) || (p->o_stride_h & 3))
     return ATF_ERR_ALIGNMENT;
+  if (p->part_stride_o < 0 || p->part_stride_lse < 0 || (p->part_stride_o & 3)) return ATF_ERR_ALIGNMENT;
+  if (p->part_indptr == nullptr &&
+      ((p->part_stride_o > 0 && p->part_stride_o < static_cast<int64_t>(p->batch) * p->num_heads * 128) ||
+       (p->part_stride_lse > 0 && p->part_stride_lse < static_cast<int64_t>(p->batch) * p->num_heads)))
+    return ATF_ERR_INVALID_ARG;
   merge::Args m;
+  m.part_stride_o = p->part_indptr == nullptr ? p->part_stride_o : 0;
+  m.part_stride_l = p->part_indptr == nullptr ? p->part_stride_lse : 0;
   m.po = p->part_o;
   m.pl = p->part_lse;
   m.indptr = p->part_indptr;

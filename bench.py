@@ -59,17 +59,59 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU during the
+    timed region. NVML is polled every 2 ms from a thread (read-only queries), so
+    short regions get samples too; without NVML, nvidia-smi is sampled instead."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, index):
+    def __init__(self, index, period_s=0.002):
         self.index = index
+        self.period = period_s
         self.proc = None
+        self.thread = None
         self.lines = []
+        self.samples = []
+        self.smax = None
+        self.nvml = None
+        self.handle = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except pynvml.NVMLError:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def _poll(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((float(sm), int(rs)))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def start(self):
+        if self.nvml is not None:
+            self._stop.clear()
+            self.samples = []
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -84,6 +126,16 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self._stop.set()
+            self.thread.join(timeout=2)
+            sm = [x for x, _ in self.samples]
+            mask = 0
+            for _, r in self.samples:
+                mask |= r
+            reasons = sorted(n for n, b in self.REASON_BITS if mask & b)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -107,7 +159,23 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
+
+
+def merge_clocks(clocks, world):
+    """Every rank's clock summary, merged on all ranks: median of the per-rank
+    medians, union of the reasons."""
+    if world == 1 or clocks is None:
+        return clocks
+    allc = [None] * world
+    dist.all_gather_object(allc, clocks)
+    meds = [c["sm_mhz"] for c in allc if c and c.get("sm_mhz") is not None]
+    maxes = [c["sm_max_mhz"] for c in allc if c and c.get("sm_max_mhz") is not None]
+    reasons = sorted(set(r for c in allc if c for r in c.get("reasons", [])))
+    return {"sm_mhz": statistics.median(meds) if meds else None, "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": reasons, "samples": sum(c.get("samples", 0) for c in allc if c),
+            "per_rank_sm_mhz": [c.get("sm_mhz") if c else None for c in allc],
+            "source": allc[0].get("source") if allc[0] else None}
 
 
 def setup_dist(n_gpus):
@@ -157,6 +225,8 @@ def timed(fn, steps, warmup, world, stream=None, sampler=None):
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
     barrier(world)
+    if sampler:
+        clocks = merge_clocks(clocks, world)
     ms = e0.elapsed_time(e1) / steps
     return max_over_ranks(ms, world), clocks
 

@@ -226,6 +226,11 @@ typedef struct {
   int64_t o_stride_b, o_stride_h;
   int out_dtype;         /* ATF_DTYPE_* */
   float* lse_out;        /* optional [B, H], natural log */
+  /* Uniform parts only: floats between consecutive parts of part_o / part_lse
+   * (0 = packed). A part's own [B, H, 128] / [B, H] block stays contiguous, so
+   * parts gathered into one flat buffer per rank merge in place. part_stride_o
+   * must be a multiple of 4. */
+  int64_t part_stride_o, part_stride_lse;
 } AtfMergeParams;
 
 /* Merge partial attention states: LSE = log sum exp(LSE_i), O = sum exp(LSE_i - LSE) O_i. */
@@ -291,6 +296,10 @@ int atf_paged_kv_append(const AtfAppendParams* p, atf_stream_t stream);
 
 const char* atf_status_string(int status);
 int atf_version(void);
+/* sizeof of the named params struct ("AtfPrefillParams", "AtfDecodePlanParams",
+ * "AtfDecodePlan", "AtfDecodeParams", "AtfMergeParams", "AtfRopeParams",
+ * "AtfAppendParams"), or -1: lets an FFI binding check its struct mirrors. */
+int64_t atf_params_size(const char* name);
 /* Synchronises the current device, copies *error_flag to *out and clears it. */
 int atf_read_error_flag(int* error_flag_device, int* out);
 

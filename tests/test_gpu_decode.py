@@ -220,6 +220,31 @@ def test_kv_sharded_decode_merge(cuda_device):
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
 
 
+def test_lse_merge_strided_parts_equal_packed(cuda_device):
+    """Parts laid out as one flat buffer per rank (O block, then the LSE block
+    padded to 4 floats), as atflash.dist all-gathers them, merge in place to the
+    same bits as the packed (P, B, H, 128) / (P, B, H) layout."""
+    import atflash
+    P, B, H, D = 3, 2, 7, 128
+    g = torch.Generator(device="cpu").manual_seed(31)
+    po = torch.randn((P, B, H, D), generator=g).to(cuda_device)
+    pl = (3 * torch.randn((P, B, H), generator=g)).to(cuda_device)
+    pl[1, 0, 2] = -float("inf")  # an empty part
+    n_o, n_l = B * H * D, (B * H + 3) // 4 * 4
+    flat = torch.full((P * (n_o + n_l),), float("nan"), device=cuda_device)
+    for r in range(P):
+        flat[r * (n_o + n_l): r * (n_o + n_l) + n_o] = po[r].reshape(-1)
+        flat[r * (n_o + n_l) + n_o: r * (n_o + n_l) + n_o + B * H] = pl[r].reshape(-1)
+    vo = flat.as_strided((P, B, H, D), (n_o + n_l, H * D, D, 1))
+    vl = flat.as_strided((P, B, H), (n_o + n_l, H, 1), n_o)
+    for dt in (torch.float32, torch.bfloat16):
+        o1, l1 = atflash.lse_merge(po, pl, out_dtype=dt, return_lse=True)
+        o2, l2 = atflash.lse_merge(vo, vl, out_dtype=dt, return_lse=True)
+        torch.cuda.synchronize()
+        assert torch.equal(o1, o2) and torch.equal(l1, l2)
+        assert not torch.isnan(o2.float()).any()
+
+
 def test_rope_pack_bit_exact(cuda_device):
     """Fused RoPE + pack equals the reference front-end (fp32 rotate_half RoPE,
     permutation, bf16) bit for bit given the same cos/sin tables."""

@@ -23,7 +23,7 @@ def _lib():
 
 def declared_functions():
     txt = open(HEADER).read()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(atf_\w+)\(", txt, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int64_t|int|const char\*)\s+(atf_\w+)\(", txt, flags=re.M)))
 
 
 def test_header_declares_the_abi():
@@ -39,6 +39,18 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
     from atflash import _ffi
     assert set(_ffi.EXPORTED) >= set(declared_functions())
+
+
+def test_params_struct_sizes_match_the_mirrors():
+    """Every params struct of the header has the size of its ctypes mirror, so a
+    field appended on one side only is caught on the CPU."""
+    from atflash import _ffi
+    lib = _lib()
+    names = re.findall(r"^\}\s+(Atf\w+);", open(HEADER).read(), flags=re.M)
+    assert "AtfMergeParams" in names and "AtfDecodeParams" in names
+    for n in names:
+        assert lib.atf_params_size(n.encode()) == ctypes.sizeof(getattr(_ffi, n)), n
+    assert lib.atf_params_size(b"NoSuchStruct") == -1
 
 
 def test_status_strings():
