@@ -520,18 +520,28 @@ def main():
         }
     # e2e through the public API with host buffers: H2D of this rank's q rows and
     # of k/v, the prefill, D2H of this rank's output rows. The copies are
-    # pipelined with the compute: k/v first, then q in chunks of E2E_CHUNK rows
-    # on a copy stream; each chunk is one flash_attn_func call (bottom-right
-    # causal via q_offset, bit-identical to one call over the block) and its
-    # output goes back on a third stream while the next chunk computes.
+    # pipelined with the compute. A chunk of query rows [c0, c1) needs keys
+    # [0, c1) only, so the copy stream sends, per chunk in ascending order, the
+    # k/v rows not sent yet and the chunk's q rows. Each chunk is one
+    # flash_attn_func call (bottom-right causal via q_offset, bit-identical to
+    # one call over the block) and its output goes back on a third stream while
+    # later chunks compute. Chunks grow from 2048 rows (short pipeline fill) to
+    # 16384 and the last one is 4096 rows (short drain).
     e2e = None
     if not args.no_extras:
-        E2E_CHUNK = 16384
         qh, kh, vh = (t.cpu().pin_memory() for t in inputs[0])
         outh = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16).pin_memory()
         qd, kd, vd = (torch.empty(t.shape, dtype=t.dtype, device=device) for t in (qh, kh, vh))
         outd = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16, device=device)
-        chunks = [(c0, min(c0 + E2E_CHUNK, e)) for (s, e) in blocks if e > s for c0 in range(s, e, E2E_CHUNK)]
+        chunks = []
+        for (bs, be) in blocks:
+            c0, size = bs, 2048
+            while c0 < be:
+                c1 = min(c0 + size, be)
+                if be - c1 < 4096 and c1 < be and be - c0 > 4096:
+                    c1 = be - 4096          # leave a short last chunk
+                chunks.append((c0, c1))
+                c0, size = c1, min(2 * size, 16384)
         h2d = (kh.numel() + vh.numel()) * 2 + sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         d2h = sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -540,11 +550,14 @@ def main():
 
         def e2e_fn(i):
             main = torch.cuda.current_stream()
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
             up.wait_stream(main)
             with torch.cuda.stream(up):
+                kv_sent = 0
                 for n, (c0, c1) in enumerate(chunks):
+                    if c1 > kv_sent:
+                        kd[:, kv_sent:c1].copy_(kh[:, kv_sent:c1], non_blocking=True)
+                        vd[:, kv_sent:c1].copy_(vh[:, kv_sent:c1], non_blocking=True)
+                        kv_sent = c1
                     qd[:, c0:c1].copy_(qh[:, c0:c1], non_blocking=True)
                     ev_q[n].record(up)
             for n, (c0, c1) in enumerate(chunks):
@@ -556,10 +569,12 @@ def main():
                 with torch.cuda.stream(down):
                     outh[:, c0:c1].copy_(outd[:, c0:c1], non_blocking=True)
             main.wait_stream(down)
+            main.wait_stream(up)
         ms_e2e, _ = timed(e2e_fn, max(2, args.steps // 2), 3, world)
         e2e = {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "pipeline": f"k/v H2D, then q in {E2E_CHUNK}-row chunks on a copy stream overlapped with "
-                           f"the chunked prefill and the D2H of each chunk's output"}
+               "pipeline": f"{len(chunks)} query chunks (2048 growing to 16384 rows, last 4096) in "
+                           f"ascending order; the copy stream sends each chunk's new k/v rows and its q "
+                           f"rows; each chunk's output D2H overlaps the later chunks' compute"}
         del qd, kd, vd, outd
     decode = None
     decode_1m = None
