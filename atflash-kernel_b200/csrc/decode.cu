@@ -376,20 +376,24 @@ namespace decode_tma {
 // as the cp.async kernel above on 16-key groups; a group never straddles two
 // slices (R >= 16).
 //
-// Shared memory of one stage: K slices at s * 256R (level l of the slice at
-// + l * 32R, SW32), then V slices at 16 KB + s * 256R (half h at + h * 128R,
-// SW128). For R = 64 this is the plain level-major / half-major layout.
+// The stage ring: a CTA's item reads at most Lc in-window levels (the depth at
+// its newest key), so its K part of a stage is Lc x 2 KB and the 96 KB ring holds
+// RING_BYTES / (Lc x 2 KB + 16 KB) stages (3 at Lc = 8, 4 at Lc <= 4, 5 at
+// Lc = 1): with fewer K bytes per stage, more stages are in flight.
+// Shared memory of one stage: K slices at s * 32 Lc R (level l of the slice at
+// + l * 32R, SW32), then V slices at Lc x 2 KB + s * 256R (half h at
+// + h * 128R, SW128). For R = 64 this is the plain level-major / half-major layout.
 constexpr int STAGE_KEYS = 64;
-constexpr int NSTAGE = 3;
+constexpr int NSTAGE_MAX = 5;
 constexpr int CONSUMERS = 4;
 constexpr int THREADS = (CONSUMERS + 1) * 32;
-constexpr uint32_t K_BYTES = STAGE_KEYS * 256;  // 64 rows x 8 levels x 16 dims
-constexpr uint32_t V_BYTES = STAGE_KEYS * 256;  // 64 rows x 128 dims
-constexpr uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
+constexpr uint32_t KLEVEL_BYTES = STAGE_KEYS * 32;  // one level of 64 rows
+constexpr uint32_t V_BYTES = STAGE_KEYS * 256;      // 64 rows x 128 dims
+constexpr uint32_t RING_BYTES = 3 * (8 * KLEVEL_BYTES + V_BYTES);  // 96 KB
 constexpr int MAX_ITEM_KEYS = 16384;  // atf_decode_plan never makes longer items
 constexpr int MAX_ITEM_PAGES = MAX_ITEM_KEYS / 16 + 1;
-constexpr uint32_t OFF_BAR = NSTAGE * STAGE_BYTES;
-constexpr uint32_t OFF_PAGES = OFF_BAR + 64;
+constexpr uint32_t OFF_BAR = RING_BYTES;
+constexpr uint32_t OFF_PAGES = OFF_BAR + 128;
 constexpr uint32_t SMEM_BYTES = OFF_PAGES + 4 * MAX_ITEM_PAGES + 1024;
 constexpr uint32_t FULLMASK = 0xffffffffu;
 
@@ -422,8 +426,8 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t sb = (raw + 1023u) & ~1023u;
   uint8_t* sp = smem_raw + (sb - raw);
   auto full_bar = [&](int s) { return sb + OFF_BAR + 8u * s; };
-  auto empty_bar = [&](int s) { return sb + OFF_BAR + 8u * (NSTAGE + s); };
-  volatile int* s_abort = reinterpret_cast<volatile int*>(sp + OFF_BAR + 8 * 2 * NSTAGE);
+  auto empty_bar = [&](int s) { return sb + OFF_BAR + 8u * (NSTAGE_MAX + s); };
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sp + OFF_BAR + 8 * 2 * NSTAGE_MAX);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int item = blockIdx.x, hk = blockIdx.y;
@@ -439,10 +443,15 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int G = a.G;
   const int hq0 = hk * G;
   const int nst = (k_end - k_beg + STAGE_KEYS - 1) / STAGE_KEYS;
+  // ring geometry of this item (the same in every role)
+  const int Lc = k_end > k_beg ? snap_levels(a, q_pos - (pos0 + k_end - 1)) : ATF_MAX_LEVELS;
+  const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
+  const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
+  const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
 
   if (tid == 0) {
     *s_abort = (args.err != nullptr && *reinterpret_cast<volatile int*>(args.err) != 0) ? 1 : 0;
-    for (int s = 0; s < NSTAGE; ++s) {
+    for (int s = 0; s < NSTAGE_MAX; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), CONSUMERS);
     }
@@ -497,7 +506,9 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int n = k0 + r0;
         const int page = s_pages[n / a.page_size - first_page];
         const int tok = n % a.page_size;
-        const uint32_t dst = sb + buf * STAGE_BYTES + (is_v ? K_BYTES : 0u) + static_cast<uint32_t>(r0) * 256u;
+        const uint32_t dst = sb + buf * STAGE_BYTES +
+                             (is_v ? K_BYTES + static_cast<uint32_t>(r0) * 256u
+                                   : static_cast<uint32_t>(r0) * 32u * static_cast<uint32_t>(Lc));
         if (is_v)
           tma_load_5d(dst, &tmV, full_bar(buf), 0, tok, 0, hk, page);
         else
@@ -534,7 +545,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     // turn a stage-relative row (lrow / vrow) into that slice's layout
     const uint32_t R = static_cast<uint32_t>(args.rows);
     const uint32_t sw = static_cast<uint32_t>(warp * 16) / R;
-    const uint32_t k_slice = sw * R * 224u, v_slice = sw * R * 128u;
+    // K slice sw starts at sw * 32 Lc R; krow below already adds 32 per stage row
+    const uint32_t k_slice = sw * R * 32u * static_cast<uint32_t>(Lc - 1), v_slice = sw * R * 128u;
     const uint32_t lstride = 32u * R, hstride = 128u * R;
     for (int s = 0; s < nst; ++s) {
       const int buf = s % NSTAGE;
