@@ -89,6 +89,10 @@ CASES = [
     ([700, 1200], 4, 2, 16, "NHD", 1e4, 2.0),       # GQA group 2
     ([2500], 16, 4, 64, "NHD", 5e5, 2.0),           # GQA group 4
     ([1800, 33], 32, 4, 16, "HND", 1e4, 2.0),       # GQA group 8
+    ([3000, 129], 8, 2, 32, "NHD", 1e4, 2.0),       # page 32
+    ([2200, 64], 28, 4, 128, "HND", 1e7, 2.0),      # page 128
+    ([4000], 24, 8, 256, "NHD", 5e5, 2.0),          # page 256
+    ([300 + 97 * i for i in range(16)], 12, 4, 16, "NHD", 1e4, 2.0),  # 16 ragged requests
 ]
 
 
