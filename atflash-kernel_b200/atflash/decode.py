@@ -191,10 +191,19 @@ class BatchDecodeWithPagedKVCacheWrapper:
         if tuple(q.shape) != (B, Hq, 128):
             raise ValueError(f"q must be ({B}, {Hq}, 128)")
         odt = out_dtype or (out.dtype if out is not None else torch.bfloat16)
+        if odt not in (torch.bfloat16, torch.float32):
+            raise TypeError("out_dtype must be bfloat16 or float32")
         if out is None:
             out = torch.empty((B, Hq, 128), dtype=odt, device=dev)
+        elif (tuple(out.shape) != (B, Hq, 128) or out.dtype != odt or out.device != q.device
+              or out.stride(-1) != 1):
+            raise ValueError(f"out must be a ({B}, {Hq}, 128) {odt} tensor on {q.device} with a "
+                             "contiguous head_dim axis")
         if return_lse and lse is None:
             lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
+        if lse is not None and (tuple(lse.shape) != (B, Hq) or lse.dtype != torch.float32
+                                or lse.device != q.device or lse.stride() != (Hq, 1)):
+            raise ValueError(f"lse must be a contiguous float32 ({B}, {Hq}) tensor on {q.device}")
         ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
         base = (ws.data_ptr() + 255) // 256 * 256
         po = base

@@ -71,6 +71,10 @@ def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bo
     zhi = resolve_zhi(window_table, D, q_offset + Sq)
     if out is None:
         out = torch.empty((B, Sq, Hq, D), dtype=torch.bfloat16, device=dev)
+    elif (tuple(out.shape) != (B, Sq, Hq, D) or out.dtype != torch.bfloat16 or out.device != q.device
+          or out.stride(-1) != 1):
+        raise ValueError(f"out must be a bf16 ({B}, {Sq}, {Hq}, {D}) tensor on {q.device} "
+                         "with a contiguous head_dim axis")
     lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=dev) if return_lse else None
     p = _ffi.AtfPrefillParams()
     p.q, p.k, p.v, p.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
@@ -108,7 +112,8 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
       kernel layout) or "rotate_half" (HF order; read in place, no permute copy).
     rope: optional (cos, sin) fp32 tables of shape (n_pos, 64); when given, q and k
       are pre-RoPE in rotate_half order and are rotated first (query i at position
-      q_offset + i, key n at position n).
+      q_offset + i, key n at position n), into the sorted-pair order the kernel
+      reads fastest.
     Returns out, or (out, softmax_lse, None) when return_attn_probs.
     """
     if dropout_p != 0.0:
@@ -121,9 +126,9 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
         cos, sin = rope
         Sq, Sk = q.shape[1], k.shape[1]
         off = (Sk - Sq) if q_offset is None else q_offset
-        q = rope_pack(q, cos, sin, pos_offset=off, out_layout="rotate_half")
-        k = rope_pack(k, cos, sin, pos_offset=0, out_layout="rotate_half")
-        qk_layout = "rotate_half"
+        q = rope_pack(q, cos, sin, pos_offset=off, out_layout="sorted_pair")
+        k = rope_pack(k, cos, sin, pos_offset=0, out_layout="sorted_pair")
+        qk_layout = "sorted_pair"
     res = prefill_fwd(q, k, v, causal=causal, softmax_scale=softmax_scale, window_table=window_table,
                       qk_layout=qk_layout, q_offset=q_offset, out=out, return_lse=return_attn_probs)
     if return_attn_probs:

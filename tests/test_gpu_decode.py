@@ -224,6 +224,21 @@ def test_kv_sharded_decode_merge(cuda_device):
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
 
 
+def test_decode_rejects_wrong_out_and_lse_buffers(cuda_device):
+    """Caller-supplied out / lse of the wrong shape or dtype are refused before any
+    launch."""
+    kv_lens, hq, hkv, page = [300, 40], 6, 2, 16
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, page, seed=41)
+    bad_outs = [torch.empty((2, hq, 64), dtype=torch.bfloat16, device=cuda_device),
+                torch.empty((2, hq, 128), dtype=torch.float16, device=cuda_device)]
+    for bad in bad_outs:
+        with pytest.raises((ValueError, TypeError)):
+            run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", None, out=bad)
+    with pytest.raises(ValueError):
+        run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", None, return_lse=True,
+                   lse=torch.empty((2, hq + 1), dtype=torch.float32, device=cuda_device))
+
+
 def test_lse_merge_strided_parts_equal_packed(cuda_device):
     """Parts laid out as one flat buffer per rank (O block, then the LSE block
     padded to 4 floats), as atflash.dist all-gathers them, merge in place to the

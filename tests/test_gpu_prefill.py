@@ -82,6 +82,21 @@ def test_prefill_parity(cuda_device, case, window):
     assert mx <= 2 * anchor + 2e-3, (mx, anchor)
 
 
+def test_prefill_rejects_a_wrong_out_buffer(cuda_device):
+    """A caller-supplied out of the wrong shape, dtype or layout is refused before
+    any launch (its strides would otherwise steer the kernel's stores)."""
+    atflash = _atf()
+    q = torch.zeros((1, 256, 4, 128), dtype=torch.bfloat16, device=cuda_device)
+    k = torch.zeros((1, 256, 2, 128), dtype=torch.bfloat16, device=cuda_device)
+    for bad in (torch.empty((1, 128, 4, 128), dtype=torch.bfloat16, device=cuda_device),
+                torch.empty((1, 256, 4, 128), dtype=torch.float32, device=cuda_device),
+                torch.empty((1, 256, 128, 4), dtype=torch.bfloat16, device=cuda_device).transpose(2, 3)):
+        with pytest.raises(ValueError):
+            atflash.prefill_fwd(q, k, k, out=bad)
+    good = torch.empty((1, 256, 4, 128), dtype=torch.bfloat16, device=cuda_device)
+    assert atflash.prefill_fwd(q, k, k, out=good) is good
+
+
 def test_prefill_batch_of_two(cuda_device):
     """Two sequences in one call (B = 2, GQA group 4): each batch row matches the
     oracle run on its own."""
