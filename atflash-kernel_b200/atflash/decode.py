@@ -53,6 +53,15 @@ class BatchDecodeWithPagedKVCacheWrapper:
 
     def reset_workspace_buffer(self, float_workspace_buffer, int_workspace_buffer=None):
         self._ws = float_workspace_buffer
+        if self._plan is not None:
+            # the planned launch parameters point into the workspace
+            P = self._plan
+            need = 4 * (P["po_floats"] + P["pl_floats"]) + 256
+            if self._ws.numel() * self._ws.element_size() < need:
+                raise ValueError(f"workspace too small for the current plan: need {need} bytes")
+            ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
+            base = (ws.data_ptr() + 255) // 256 * 256
+            self._tmpl.partial_o, self._tmpl.partial_lse = base, base + 4 * P["po_floats"]
 
     def plan(self, indptr, indices, last_page_len, num_qo_heads: int, num_kv_heads: int,
              head_dim: int, page_size: int, pos_encoding_mode: str = "NONE", window_left: int = -1,
@@ -143,6 +152,28 @@ class BatchDecodeWithPagedKVCacheWrapper:
             "window": mode, "zhi16": zhi16, "zhi8": zhi8, "layout": _LAYOUTS[qk_layout],
             "kv_lens": kv_lens,
         }
+        # everything of the launch parameters that the plan fixes, filled once;
+        # run() copies this template and sets the per-call pointers only
+        P = self._plan
+        t = _ffi.AtfDecodeParams()
+        t.kv_layout = _ffi.ATF_KV_NHD if self._kv_layout == "NHD" else _ffi.ATF_KV_HND
+        t.qk_layout = P["layout"]
+        t.indptr, t.indices = P["indptr"].data_ptr(), P["indices"].data_ptr()
+        t.last_page_len = P["last_page_len"].data_ptr()
+        t.items, t.item_indptr, t.num_items = P["items"].data_ptr(), P["item_indptr"].data_ptr(), P["num_items"]
+        t.batch_size, t.num_qo_heads, t.num_kv_heads, t.head_dim, t.page_size = B, num_qo_heads, num_kv_heads, 128, \
+            page_size
+        t.sm_scale = P["sm_scale"]
+        t.window = P["window"]
+        for i in range(8):
+            t.zhi16[i] = zhi16[i]
+        for i in range(16):
+            t.zhi8[i] = zhi8[i]
+        ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
+        base = (ws.data_ptr() + 255) // 256 * 256
+        t.partial_o, t.partial_lse = base, base + 4 * P["po_floats"]
+        t.error_flag = _runtime.error_flag(dev).data_ptr()
+        self._tmpl = t
 
     begin_forward = plan
 
@@ -204,21 +235,11 @@ class BatchDecodeWithPagedKVCacheWrapper:
         if lse is not None and (tuple(lse.shape) != (B, Hq) or lse.dtype != torch.float32
                                 or lse.device != q.device or lse.stride() != (Hq, 1)):
             raise ValueError(f"lse must be a contiguous float32 ({B}, {Hq}) tensor on {q.device}")
-        ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
-        base = (ws.data_ptr() + 255) // 256 * 256
-        po = base
-        pl = base + 4 * P["po_floats"]
-        a = _ffi.AtfDecodeParams()
+        a = _ffi.AtfDecodeParams.from_buffer_copy(self._tmpl)
         a.q, a.q_stride_b, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
         a.k_cache, a.v_cache = kc.data_ptr(), vc.data_ptr()
         a.num_pages = kc.shape[0]
         a.kv_stride_page, a.kv_stride_token, a.kv_stride_head = s_page, s_tok, s_head
-        a.kv_layout = _ffi.ATF_KV_NHD if self._kv_layout == "NHD" else _ffi.ATF_KV_HND
-        a.qk_layout = P["layout"]
-        a.indptr, a.indices = P["indptr"].data_ptr(), P["indices"].data_ptr()
-        a.last_page_len = P["last_page_len"].data_ptr()
-        a.items, a.item_indptr, a.num_items = P["items"].data_ptr(), P["item_indptr"].data_ptr(), P["num_items"]
-        a.batch_size, a.num_qo_heads, a.num_kv_heads, a.head_dim, a.page_size = B, Hq, P["Hkv"], 128, page
         keep = []
         if q_pos is not None:
             q_pos = q_pos.to(device=dev, dtype=torch.int64).contiguous()
@@ -228,17 +249,9 @@ class BatchDecodeWithPagedKVCacheWrapper:
             kv_pos0 = kv_pos0.to(device=dev, dtype=torch.int64).contiguous()
             keep.append(kv_pos0)
             a.kv_pos0 = kv_pos0.data_ptr()
-        a.sm_scale = P["sm_scale"]
-        a.window = P["window"]
-        for i in range(8):
-            a.zhi16[i] = P["zhi16"][i]
-        for i in range(16):
-            a.zhi8[i] = P["zhi8"][i]
-        a.partial_o, a.partial_lse = po, pl
         a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
         a.out_dtype = _ffi.ATF_DTYPE_F32 if out.dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
         a.lse_out = lse.data_ptr() if lse is not None else None
-        a.error_flag = _runtime.error_flag(dev).data_ptr()
         if k_level_major:
             a.k_level_major = 1
             a.k_stride_page, a.k_stride_head, a.k_stride_level = kc.stride(0), kc.stride(1), kc.stride(2)
