@@ -163,3 +163,78 @@ def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Ten
     wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=o_view, lse=l_view, return_lse=True,
                 out_dtype=torch.float32)
     return _gather_and_merge(pack, B, H, D, group, world, None, out_dtype)
+
+
+class ShardedDecodeStep:
+    """A KV-sharded decode step with fixed buffers, replayed from CUDA graphs.
+
+    This rank's split-KV decode (and its own merge) is captured as one graph and
+    the cross-rank LSE merge as another. The NCCL all-gather between them runs
+    eagerly on the same stream, so no collective is captured in a graph. The
+    caller writes each step's query into ``self.q`` (a copy of `q`, made at
+    construction); `q_pos` / `kv_pos0` must be device tensors and may also be
+    updated in place. Calling the object runs one step and returns (out, lse),
+    tensors that later steps overwrite. The result equals ``sharded_decode`` on
+    the same inputs bit for bit.
+    """
+
+    def __init__(self, q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
+                 kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16):
+        if not (q_pos.is_cuda and kv_pos0.is_cuda):
+            raise ValueError("q_pos and kv_pos0 must be CUDA tensors (they are read by the replayed graph)")
+        _, self.world = _rank_world(group)
+        self.group = group
+        self.q = q.clone()
+        self.q_pos, self.kv_pos0 = q_pos, kv_pos0
+        B, H, D = q.shape
+        self.B, self.H, self.D = B, H, D
+        self.pack, self.o_view, self.l_view = _pack_views(B, H, D, q.device)
+        n = self.pack.numel()
+        self.allp = self.pack.new_empty((self.world * n,))
+        from .decode import lse_merge
+
+        def local():
+            if self.world == 1:
+                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                                   out_dtype=out_dtype)
+            wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=self.o_view, lse=self.l_view,
+                        return_lse=True, out_dtype=torch.float32)
+            return None
+
+        def merge():
+            po = self.allp.as_strided((self.world, B, H, D), (n, H * D, D, 1))
+            pl = self.allp.as_strided((self.world, B, H), (n, H, 1), B * H * D)
+            return lse_merge(po, pl, lse_log2=False, out_dtype=out_dtype, return_lse=True)
+
+        # one eager step first (library load, lazy allocations), then the captures
+        local()
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.allp, self.pack, group=group)
+            merge()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(q.device)
+        side.wait_stream(torch.cuda.current_stream())
+        self.g_local = torch.cuda.CUDAGraph()
+        self.g_merge = None
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(self.g_local):
+                res = local()
+            if self.world > 1:
+                self.g_merge = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.g_merge):
+                    res = merge()
+        torch.cuda.current_stream().wait_stream(side)
+        self.out, self.lse = res
+
+    def __call__(self):
+        self.g_local.replay()
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.allp, self.pack, group=self.group)
+            self.g_merge.replay()
+        return self.out, self.lse
+
+    def release(self):
+        """Free the graphs (before the process group is destroyed)."""
+        self.g_local = None
+        self.g_merge = None
+

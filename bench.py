@@ -406,9 +406,17 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
         agg = total / (ms * 1e-3) / 1e9
         res[name] = {"us": ms * 1e3, "bytes_total": total, "gbs_aggregate": agg,
                      "hbm_frac_per_gpu": agg / (world * peaks["hbm_gbs"])}
+        # the same step from atflash.dist.ShardedDecodeStep: the rank's decode and the
+        # cross-rank merge replay as CUDA graphs, the all-gather runs eagerly between
+        step = atflash.dist.ShardedDecodeStep(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0)
+        ms_g, _ = timed(lambda i: step(), steps, warmup, world)
+        step.release()
+        res[name]["us_graph"] = ms_g * 1e3
+        res[name]["gbs_aggregate_graph"] = total / (ms_g * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
     res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, KV split into {world} shards, "
-                     "all-gather of (O, LSE) + LSE merge inside the step")
+                     "all-gather of (O, LSE) + LSE merge inside the step; us: eager "
+                     "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep")
     del kc, vc
     torch.cuda.empty_cache()
     return res

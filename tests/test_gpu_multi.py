@@ -94,6 +94,20 @@ def _worker(rank, world, port, errq):
         torch.cuda.synchronize()
         err = (out - ref).abs().max().item()
         assert err < 2e-3, f"sharded decode differs from the one-GPU decode by {err}"
+        # the same step replayed from CUDA graphs (the all-gather stays eager)
+        step = atflash.dist.ShardedDecodeStep(qd, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                              out_dtype=torch.float32)
+        for _ in range(2):
+            o_g, l_g = step()
+        torch.cuda.synchronize()
+        assert torch.equal(o_g, out) and torch.equal(l_g, lse), "graph step differs from sharded_decode"
+        step.q.copy_(torch.randn(qd.shape, generator=g).to(torch.bfloat16).to(dev))
+        o_g, l_g = step()
+        out2, lse2 = atflash.dist.sharded_decode(step.q, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                                 out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert torch.equal(o_g, out2) and torch.equal(l_g, lse2), "graph step on a new query differs"
+        step.release()
         assert atflash.check_device_errors() == 0
         dist.barrier()
         dist.destroy_process_group()
