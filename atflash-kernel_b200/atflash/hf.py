@@ -35,7 +35,7 @@ from .prefill import prefill_fwd
 # FlashAttention path, hence a name without it (as the reference notes).
 DEFAULT_NAME = "atf_window"
 
-_STATE = {"prefill": None, "decode": None, "ws": {}}
+_STATE = {"prefill": None, "decode": None, "ws": {}, "plans": {}}
 
 
 def window_tables_for_model(model, k_ret_prefill: float, k_ret_decode: Optional[float] = None,
@@ -68,6 +68,7 @@ def configure(prefill: Optional[WT.WindowTable], decode: Optional[WT.WindowTable
     """Set the windows the attention function uses (None: dense)."""
     _STATE["prefill"] = prefill
     _STATE["decode"] = decode
+    _STATE["plans"].clear()
 
 
 def _workspace(dev) -> torch.Tensor:
@@ -112,11 +113,18 @@ def _decode(query, key, value, scaling):
         vc = vc.contiguous()
         kc = kc.contiguous()
     dev = query.device
-    w = BatchDecodeWithPagedKVCacheWrapper(_workspace(dev), kv_layout="HND")
-    indptr = torch.arange(b + 1, dtype=torch.int32)
-    w.plan(indptr, torch.arange(b, dtype=torch.int32), torch.full((b,), S, dtype=torch.int32), hq, hkv, d, S,
-           window_table=_STATE["decode"], qk_layout="rotate_half",
-           sm_scale=scaling if scaling is not None else 1.0 / math.sqrt(d))
+    # every layer of one decode step has the same shapes: plan once per step
+    # (the last planned shape is kept; a new length replaces it)
+    key = (dev, b, hq, hkv, d, S, scaling)
+    w = _STATE["plans"].get(key)
+    if w is None:
+        w = BatchDecodeWithPagedKVCacheWrapper(_workspace(dev), kv_layout="HND")
+        indptr = torch.arange(b + 1, dtype=torch.int32)
+        w.plan(indptr, torch.arange(b, dtype=torch.int32), torch.full((b,), S, dtype=torch.int32), hq, hkv, d, S,
+               window_table=_STATE["decode"], qk_layout="rotate_half",
+               sm_scale=scaling if scaling is not None else 1.0 / math.sqrt(d))
+        _STATE["plans"].clear()
+        _STATE["plans"][key] = w
     out = w.run(query[:, :, 0, :], (kc, vc))           # (b, hq, d)
     return out.view(b, 1, hq, d)
 
