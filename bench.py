@@ -205,6 +205,22 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def e2e_chunks(blocks, first=2048, largest=16384, last=4096):
+    """Query-row chunks of the e2e leg, in ascending order: each block [bs, be)
+    is cut into chunks that double from `first` rows to `largest`, with a short
+    last chunk of `last` rows (a short pipeline fill and drain)."""
+    chunks = []
+    for (bs, be) in blocks:
+        c0, size = bs, first
+        while c0 < be:
+            c1 = min(c0 + size, be)
+            if be - c1 < last and c1 < be and be - c0 > last:
+                c1 = be - last          # leave a short last chunk
+            chunks.append((c0, c1))
+            c0, size = c1, min(2 * size, largest)
+    return chunks
+
+
 def timed(fn, steps, warmup, world, stream=None, sampler=None):
     """W warm-up calls, then K calls between two barriers + syncs, timed with
     CUDA events on the launching stream; returns ms per step (max over ranks)."""
@@ -543,15 +559,7 @@ def main():
         # while the previous step (on the other set) still computes
         sets = [tuple(torch.empty(t.shape, dtype=t.dtype, device=device) for t in (qh, kh, vh, qh))
                 for _ in range(2)]
-        chunks = []
-        for (bs, be) in blocks:
-            c0, size = bs, 2048
-            while c0 < be:
-                c1 = min(c0 + size, be)
-                if be - c1 < 4096 and c1 < be and be - c0 > 4096:
-                    c1 = be - 4096          # leave a short last chunk
-                chunks.append((c0, c1))
-                c0, size = c1, min(2 * size, 16384)
+        chunks = e2e_chunks(blocks)
         h2d = (kh.numel() + vh.numel()) * 2 + sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         d2h = sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
