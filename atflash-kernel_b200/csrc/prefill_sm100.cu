@@ -4,8 +4,8 @@
 // streams 128-key K/V tiles over its causal range:
 //
 //   warp 8       TMA producer. Q once (8 levels x 2 halves per tile); per key
-//                tile the K boxes that hold the in-window levels (L =
-//                D_eff/16 of the nearer query tile) and the two 64-dim V boxes.
+//                tile only the in-window K levels (L = D_eff/16 of the nearer
+//                query tile) and the two 64-dim V boxes.
 //   warp 9       MMA issuer and TMEM owner (512 columns). For key tile j:
 //                O_0 += P_0(j) V_j, S_0(j+1) = Q_0 K_{j+1}^T, then the same for
 //                Q1, so each query tile's softmax overlaps the other tile's MMAs.
@@ -33,12 +33,12 @@
 //      K-major layout: two halves (dims 0-7 and 8-15 of the level), each
 //      128 rows x 16 B, so core matrices (8 rows x 16 B) are contiguous:
 //      LBO (K direction) = 2 KB, SBO (8-row groups) = 128 B.
-//   K  2 stages x 32 KB. sorted-pair: whole 128-byte rows, two boxes (dims
-//      0-63, 64-127) x 128 keys x 128 B, 128B swizzle, K-major: level i is
-//      box i/4 at a 32-byte offset (i%4) inside the row (SBO = 1 KB); box 1 is
-//      loaded only when L > 4. Two boxes per key tile instead of 2L narrow
-//      ones cut the TMA issue work. rotate_half: 8 slabs x 4 KB in the Q
-//      layout (a level is two 8-dim chunks 64 dims apart).
+//   K  2 stages x 8 slabs x 4 KB, one slab per in-window level; only the L
+//      in-window levels are loaded. sorted-pair: one 5-d box {16 dims, 128
+//      keys, L levels} per key tile (level i is dims 16i..16i+15), slabs of
+//      128 keys x 32 B with 32-byte swizzle, K-major (SBO = 256 B).
+//      rotate_half: two 8-dim boxes per level (chunks 7-i and 15-i), in the Q
+//      slab layout.
 //   V  2 stages x 2 boxes (dims 0-63, 64-127) x 128 keys x 128 B, 128B swizzle;
 //      the PV B operand is MN-major: LBO (next 64 dims) = 16 KB, SBO (next 8
 //      keys) = 1 KB.
@@ -82,8 +82,7 @@ __device__ __forceinline__ void pv_group_asm(uint32_t o_tmem, uint32_t p_tmem, u
       : "memory");
 }
 // one elected lane issues the L (1..8) QK MMAs of a tile and the commit; level
-// i advances A by 4 KB and B by 4 KB (descriptor start field += 256): the
-// rotate_half K layout, whose slabs match Q's
+// i advances A and B by one 4 KB slab (descriptor start field += 256)
 __device__ __forceinline__ void qk_group_asm(uint32_t d_tmem, uint64_t qd, uint64_t kd, uint32_t idesc, int L,
                                              uint32_t bar_addr) {
   asm volatile(
@@ -111,37 +110,6 @@ __device__ __forceinline__ void qk_group_asm(uint32_t d_tmem, uint64_t qd, uint6
       ::"r"(d_tmem), "l"(qd), "l"(kd), "r"(idesc), "r"(L), "r"(bar_addr)
       : "memory");
 }
-// Sorted-pair K as whole 128-byte rows (two 64-dim boxes, 128B swizzle): level
-// i is box i/4 at a 32-byte offset (i%4) inside the row. A (Q level slab) still
-// advances 4 KB per level.
-__device__ __forceinline__ void qk_group_sw128_asm(uint32_t d_tmem, uint64_t qd, uint64_t kd, uint32_t idesc, int L,
-                                                   uint32_t bar_addr) {
-  asm volatile(
-      "{\n\t.reg .pred pe, p1, p2, p3, p4, p5, p6, p7;\n\t.reg .b64 a, b;\n\t"
-      "elect.sync _|pe, 0xffffffff;\n\t"
-      "setp.gt.and.s32 p1, %4, 1, pe;\n\tsetp.gt.and.s32 p2, %4, 2, pe;\n\tsetp.gt.and.s32 p3, %4, 3, pe;\n\t"
-      "setp.gt.and.s32 p4, %4, 4, pe;\n\tsetp.gt.and.s32 p5, %4, 5, pe;\n\tsetp.gt.and.s32 p6, %4, 6, pe;\n\t"
-      "setp.gt.and.s32 p7, %4, 7, pe;\n\t"
-      "@pe tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n\t"
-      "add.u64 a, %1, 256;\n\tadd.u64 b, %2, 2;\n\t"
-      "@p1 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, b, 2;\n\t"
-      "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, b, 2;\n\t"
-      "@p3 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, %2, 1024;\n\t"
-      "@p4 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, b, 2;\n\t"
-      "@p5 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, b, 2;\n\t"
-      "@p6 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "add.u64 a, a, 256;\n\tadd.u64 b, b, 2;\n\t"
-      "@p7 tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, 1;\n\t"
-      "@pe tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
-      ::"r"(d_tmem), "l"(qd), "l"(kd), "r"(idesc), "r"(L), "r"(bar_addr)
-      : "memory");
-}
-
 constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
 constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
 constexpr uint32_t QHALF_BYTES = BM * 16;             // 2 KB
@@ -150,7 +118,12 @@ constexpr uint32_t QTILE_BYTES = 8 * QSLAB_BYTES;     // 32 KB
 constexpr uint32_t KHALF_BYTES = BN * 16;             // 2 KB
 constexpr uint32_t KSLAB_BYTES = 2 * KHALF_BYTES;     // 4 KB
 constexpr uint32_t KSTAGE_BYTES = 8 * KSLAB_BYTES;    // 32 KB
-constexpr uint32_t KBOX128_BYTES = BN * 128;          // 16 KB: 128 keys x 64 dims
+// sorted-pair K tensor maps over (16 dims of a level, key, level, kv head,
+// batch); map L-1 moves the box {16, 128, L}: exactly the L in-window levels,
+// as [L][128 keys][32 B] with 32-byte swizzle
+struct KLevelMaps {
+  CUtensorMap lv[ATF_MAX_LEVELS];
+};
 constexpr uint32_t VBOX_BYTES = BN * 128;             // 16 KB
 constexpr uint32_t VSTAGE_BYTES = 2 * VBOX_BYTES;     // 32 KB
 constexpr uint32_t OFF_Q = 0;
@@ -226,7 +199,7 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmK128,
+                   const __grid_constant__ KLevelMaps tmKL,
                    const __grid_constant__ CUtensorMap tmV, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -288,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == WARP_LOAD && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmK128);
+    for (int L = 0; L < ATF_MAX_LEVELS; ++L) tma_prefetch_desc(&tmKL.lv[L]);
     tma_prefetch_desc(&tmV);
   }
   if (warp == WARP_MMA) {
@@ -337,11 +310,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       const uint32_t kdst = sb + OFF_K + ks * KSTAGE_BYTES;
       if (a.layout == ATF_LAYOUT_SORTED_PAIR) {
-        // levels 0-3 are dims 0-63 (box 0), levels 4-7 dims 64-127 (box 1)
-        const int nbox = L > 4 ? 2 : 1;
-        mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(nbox) * KBOX128_BYTES);
-        tma_load_4d_elect(kdst, &tmK128, bar(B_KFULL + ks), 0, j * BN, hk, bi);
-        if (nbox > 1) tma_load_4d_elect(kdst + KBOX128_BYTES, &tmK128, bar(B_KFULL + ks), 64, j * BN, hk, bi);
+        // one 5-d box: the L in-window levels (dims 0..16L-1), one 4 KB slab each
+        mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
+        if (elect_one_lane()) tma_load_5d(kdst, &tmKL.lv[L - 1], bar(B_KFULL + ks), 0, j * BN, 0, hk, bi);
+        __syncwarp();
       } else {
         // rotate_half: a level is two 8-dim chunks 64 dims apart, one box each
         mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
@@ -376,7 +348,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tm = __shfl_sync(FULL, tmem, 0);
     const uint64_t qdesc0 = make_sdesc(sb + OFF_Q, QHALF_BYTES, 128, kLayoutNone);
     const uint64_t kdesc0 = make_sdesc(sb + OFF_K, KHALF_BYTES, 128, kLayoutNone);
-    const uint64_t kdesc128 = make_sdesc(sb + OFF_K, 16, 1024, kLayoutSw128);
+    // sorted-pair K level slabs: 128 keys x 32 B, 32-byte swizzle (SBO = 8 rows)
+    const uint64_t kdesc32 = make_sdesc(sb + OFF_K, 16, 256, kLayoutSw32);
     const bool sorted = a.layout == ATF_LAYOUT_SORTED_PAIR;
     const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
     auto issue_S = [&](int t, int j) {
@@ -384,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
       const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
       if (sorted)
-        qk_group_sw128_asm(d_tmem, qd, kdesc128 + (((j % KST) * KSTAGE_BYTES) >> 4), IDESC_QK, L, bar(B_SFULL + t));
+        qk_group_asm(d_tmem, qd, kdesc32 + (((j % KST) * KSTAGE_BYTES) >> 4), IDESC_QK, L, bar(B_SFULL + t));
       else
         qk_group_asm(d_tmem, qd, kdesc0 + (((j % KST) * KSTAGE_BYTES) >> 4), IDESC_QK, L, bar(B_SFULL + t));
     };
@@ -611,7 +584,8 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
 
-  CUtensorMap tq, tk, tk128, tv;
+  CUtensorMap tq, tk, tv;
+  KLevelMaps tkl;
   auto sane = [](int64_t stride, int64_t size) -> uint64_t {
     // Size-1 dims may carry any stride; use a valid placeholder.
     return static_cast<uint64_t>(size == 1 ? 16 : stride * 2);
@@ -631,9 +605,16 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     const uint32_t box[4] = {8, static_cast<uint32_t>(BN), 1, 1};
     if ((rc = encode_tiled_bf16(&tk, p->k, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != ATF_OK)
       return rc;
-    const uint32_t box128[4] = {64, static_cast<uint32_t>(BN), 1, 1};
-    if ((rc = encode_tiled_bf16(&tk128, p->k, 4, dims, str, box128, CU_TENSOR_MAP_SWIZZLE_128B)) != ATF_OK)
-      return rc;
+    // (16 dims, key, level, kv head, batch): the level axis is a view of head_dim
+    const uint64_t dims5[5] = {16, (uint64_t)p->seqlen_k, ATF_MAX_LEVELS, (uint64_t)p->num_heads_kv,
+                               (uint64_t)p->batch};
+    const uint64_t str5[4] = {sane(p->k_stride_s, p->seqlen_k), 32, sane(p->k_stride_h, p->num_heads_kv),
+                              sane(p->k_stride_b, p->batch)};
+    for (int L = 1; L <= ATF_MAX_LEVELS; ++L) {
+      const uint32_t box5[5] = {16, static_cast<uint32_t>(BN), static_cast<uint32_t>(L), 1, 1};
+      if ((rc = encode_tiled_bf16(&tkl.lv[L - 1], p->k, 5, dims5, str5, box5, CU_TENSOR_MAP_SWIZZLE_32B)) != ATF_OK)
+        return rc;
+    }
   }
   {
     const uint64_t dims[4] = {128, (uint64_t)p->seqlen_k, (uint64_t)p->num_heads_kv, (uint64_t)p->batch};
@@ -670,6 +651,6 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
   const long long grid = static_cast<long long>(a.n_qblk) * a.B * a.Hq;
   if (grid > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
   prefill_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES,
-                   reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tk128, tv, a);
+                   reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tkl, tv, a);
   return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
 }

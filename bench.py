@@ -44,8 +44,8 @@ N_CTX, HQ, HKV, D, THETA, K_RET = 131072, 28, 4, 128, 1e7, 2.0
 METRIC = "Windowed-attn prefill ms @128K/512K + decode µs/step @128K, window on vs off"
 # dram__bytes_read.sum + dram__bytes_write.sum of one 131072-token k=2 prefill
 # launch, from a one-pass ncu capture of the full-size launch (summarised under
-# profiles/ with its command): 2.254 GB read + 0.902 GB written
-PREFILL_TRAFFIC_BYTES = 2.254e9 + 0.902e9
+# profiles/ with its command): 2.282 GB read + 0.902 GB written
+PREFILL_TRAFFIC_BYTES = 2.282e9 + 0.902e9
 
 
 def load_peaks():
