@@ -136,9 +136,21 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
     return res
 
 
+_FA4_TUNING_SUFFIXES = ("_block_size", "num_threads", "num_stages", "_compute_capability")
+
+
 def _flash_attn_fwd(q, k, v, softmax_scale=None, causal=False, pack_gqa=None,
-                    atflash_window_zhi=None, **unused):
+                    atflash_window_zhi=None, **other):
     """Drop-in for the windowed FA4 entry point the reference calls
-    (``flash_attn.cute.interface._flash_attn_fwd``): returns (out, lse)."""
+    (``flash_attn.cute.interface._flash_attn_fwd``): returns (out, lse).
+
+    ``pack_gqa`` and FA4's tile-size / thread-count hints are accepted and
+    ignored: this kernel always packs the G q heads of a kv head together.
+    Any other FA4 option (varlen, paged K/V, softcap, sliding window, sinks)
+    must be left at None; a value raises NotImplementedError instead of being
+    dropped silently."""
+    for name, value in other.items():
+        if value is not None and not name.endswith(_FA4_TUNING_SUFFIXES):
+            raise NotImplementedError(f"_flash_attn_fwd: {name}={value!r} is not supported by the windowed prefill")
     return prefill_fwd(q, k, v, causal=causal, softmax_scale=softmax_scale,
                        window_table=atflash_window_zhi, return_lse=True)

@@ -153,3 +153,21 @@ def test_append_rejects_bad_arguments_without_gpu():
     p.cos = None
     p.a_stride_n = 3  # misaligned token stride
     assert lib.atf_paged_kv_append(ctypes.byref(p), None) == -3
+
+
+def test_fa4_entry_rejects_unsupported_options_before_any_launch():
+    """The FA4-shaped entry accepts the reference's own arguments and FA4's tuning
+    hints, but refuses options it cannot honour instead of dropping them."""
+    import torch
+    import atflash
+    q = torch.zeros((1, 4, 2, 128), dtype=torch.bfloat16)
+    for name, value in (("softcap", 30.0), ("window_size_left", 128), ("cu_seqlens_q", q),
+                        ("page_table", q)):
+        with pytest.raises(NotImplementedError, match=name):
+            atflash._flash_attn_fwd(q, q, q, causal=True, **{name: value})
+    # defaults and tuning hints pass the check and reach the device check (no GPU here)
+    if not torch.cuda.is_available():
+        with pytest.raises(Exception) as e:
+            atflash._flash_attn_fwd(q, q, q, causal=True, pack_gqa=True, softcap=None,
+                                    m_block_size=128, num_threads=384)
+        assert not isinstance(e.value, NotImplementedError)
