@@ -135,6 +135,8 @@ class BatchDecodeWithPagedKVCacheWrapper:
                              else [int(x) for x in window_table])
                 if len(zhi16) != 8:
                     raise ValueError("a zhi level table has 8 entries")
+                if any(zhi16[i] < zhi16[i + 1] for i in range(7)) or min(zhi16) < 0:
+                    raise ValueError("zhi levels must be non-negative and non-increasing")
                 zhi16[0] = max(zhi16[0], KERNEL_CAP)
                 mode = _ffi.ATF_WINDOW_SNAP16
         kv_lens = [(int(indptr_h[b + 1] - indptr_h[b]) - 1) * page_size + int(lpl_h[b])

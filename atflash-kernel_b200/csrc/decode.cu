@@ -943,6 +943,9 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   if (p->window < ATF_WINDOW_OFF || p->window > ATF_WINDOW_VEC8) return ATF_ERR_INVALID_ARG;
   if (p->qk_layout != ATF_LAYOUT_SORTED_PAIR && p->qk_layout != ATF_LAYOUT_ROTATE_HALF)
     return ATF_ERR_INVALID_ARG;
+  if (p->window == ATF_WINDOW_SNAP16)  // level i + 1 is never wider than level i
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i)
+      if (p->zhi16[i] < 0 || (i > 0 && p->zhi16[i] > p->zhi16[i - 1])) return ATF_ERR_INVALID_ARG;
   if (!aligned16(p->k_cache) || !aligned16(p->v_cache) || (p->kv_stride_page & 7) ||
       (p->kv_stride_token & 7) || (p->kv_stride_head & 7))
     return ATF_ERR_ALIGNMENT;

@@ -576,7 +576,7 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     if (strides[i] < 0 || (strides[i] & 7) != 0) return ATF_ERR_ALIGNMENT;
   if (p->window == ATF_WINDOW_SNAP16) {
     for (int i = 0; i < ATF_MAX_LEVELS; ++i)
-      if (p->zhi[i] < 0) return ATF_ERR_INVALID_ARG;
+      if (p->zhi[i] < 0 || (i > 0 && p->zhi[i] > p->zhi[i - 1])) return ATF_ERR_INVALID_ARG;
     // zhi[0] must cover the largest distance in the problem (D_eff >= 16 always).
     if (static_cast<int64_t>(p->zhi[0]) < p->q_offset + p->seqlen_q - 1) return ATF_ERR_INVALID_ARG;
   }

@@ -78,6 +78,19 @@ def test_invalid_arguments_rejected_without_gpu():
     p.softmax_scale = 0.1
     p.q = 17
     assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -3  # misaligned
+    p.q = 16
+    p.window = _ffi.ATF_WINDOW_SNAP16
+    for i, z in enumerate((100, 50, 60, 10, 0, 0, 0, 0)):
+        p.zhi[i] = z
+    assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -1  # levels must not widen
+    d = _ffi.AtfDecodeParams()
+    d.q = d.k_cache = d.v_cache = d.indptr = d.indices = d.last_page_len = 16
+    d.items = d.item_indptr = d.partial_o = d.partial_lse = d.out = 16
+    d.head_dim, d.batch_size, d.num_qo_heads, d.num_kv_heads, d.page_size = 128, 1, 8, 8, 16
+    d.window = _ffi.ATF_WINDOW_SNAP16
+    for i, z in enumerate((100, 50, 60, 10, 0, 0, 0, 0)):
+        d.zhi16[i] = z
+    assert lib.atf_decode_run(ctypes.byref(d), None) == -1
     assert lib.atf_decode_run(None, None) == -1
     assert lib.atf_lse_merge(None, None) == -1
     assert lib.atf_rope_pack(None, None) == -1
