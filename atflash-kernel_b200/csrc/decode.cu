@@ -731,6 +731,8 @@ struct Args {
   const float* pl;
   const int* indptr;
   int P, B, H;
+  // ragged parts: part indices read through indptr are clamped to [0, max_part)
+  int max_part;
   // uniform parts: floats between consecutive parts of po / pl (0: packed
   // [P, B, H, 128] / [P, B, H])
   long long part_stride_o, part_stride_l;
@@ -760,8 +762,8 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
   // part i of this (b, h): O at po + ob + i * so, LSE at pl[lb + i * sl] (floats)
   long long lb, sl, ob, so;
   if (a.indptr != nullptr) {
-    p0 = a.indptr[b];
-    p1 = a.indptr[b + 1];
+    p0 = min(max(a.indptr[b], 0), a.max_part);
+    p1 = min(max(a.indptr[b + 1], p0), a.max_part);
     lb = static_cast<long long>(p0) * a.H + h;
     sl = a.H;
     ob = lb * 128;
@@ -951,6 +953,12 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
     return ATF_ERR_ALIGNMENT;
   if ((reinterpret_cast<uintptr_t>(p->q) & 3) || (p->q_stride_b & 1) || (p->q_stride_h & 1))
     return ATF_ERR_ALIGNMENT;
+  // the split kernel stores float4 rows into partial_o; the merge stores float4
+  // (fp32 out) or 4 x bf16 (bf16 out) per lane
+  if (!aligned16(p->partial_o) || (reinterpret_cast<uintptr_t>(p->partial_lse) & 3) ||
+      (p->out_dtype == ATF_DTYPE_F32 && !aligned16(p->out)) || (reinterpret_cast<uintptr_t>(p->out) & 7) ||
+      (p->o_stride_b & 3) || (p->o_stride_h & 3))
+    return ATF_ERR_ALIGNMENT;
   int dev = 0;
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
@@ -1052,6 +1060,7 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   m.po = p->partial_o;
   m.pl = p->partial_lse;
   m.indptr = p->item_indptr;
+  m.max_part = p->num_items;
   m.P = 0;
   m.B = p->batch_size;
   m.H = p->num_qo_heads;
@@ -1084,6 +1093,7 @@ extern "C" int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream) {
   m.po = p->part_o;
   m.pl = p->part_lse;
   m.indptr = p->part_indptr;
+  m.max_part = 0x7fffffff;
   m.P = p->num_parts;
   m.B = p->batch;
   m.H = p->num_heads;

@@ -26,23 +26,75 @@ constexpr long long kPartialOFloats = kMaxRows * ATF_HEAD_DIM;
 static __device__ __align__(256) float g_decode_scratch[kPartialOFloats + kMaxRows];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-float* g_scratch_ptr[kMaxDevices] = {};
 
-// Looks the scratch address up once per device. The lookup can load this
-// library's device code into the current context, which is why the first call
-// on a device has to come before any stream capture.
+// The scratch address belongs to the context that was current when it was
+// looked up. A context is identified by cuCtxGetId, which is unique for the
+// life of the process, so a device reset (a new primary context) or a
+// non-primary context made current by the caller is seen as a new context and
+// the address is looked up again; a stale address is never handed to a kernel.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+struct ScratchSlot {
+  unsigned long long ctx_id;  // 0: not looked up yet
+  float* ptr;
+};
+std::mutex g_mu;
+ScratchSlot g_slot[kMaxDevices] = {};
+
+int load_driver_entry_points() {
+  if (g_ctx_get_current != nullptr && g_ctx_get_id != nullptr) return ATF_OK;
+  void* f1 = nullptr;
+  void* f2 = nullptr;
+  cudaDriverEntryPointQueryResult q1, q2;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+      q1 != cudaDriverEntryPointSuccess ||
+      cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+      q2 != cudaDriverEntryPointSuccess) {
+    cudaGetLastError();
+    return ATF_ERR_CUDA;
+  }
+  g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+  g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+  return ATF_OK;
+}
+
+// Id of the context current on this thread, 0 when there is none yet.
+int current_ctx_id(unsigned long long* id) {
+  CUcontext c = nullptr;
+  *id = 0;
+  if (g_ctx_get_current(&c) != CUDA_SUCCESS) return ATF_ERR_CUDA;
+  if (c == nullptr) return ATF_OK;
+  return g_ctx_get_id(c, id) == CUDA_SUCCESS ? ATF_OK : ATF_ERR_CUDA;
+}
+
+// Scratch address in the current context of `dev`, looked up with
+// cudaGetSymbolAddress the first time a context is seen. The lookup can load
+// this library's device code into that context, which is why the first call in
+// a context has to come before any stream capture.
 int scratch_for_device(int dev, float** out) {
   std::lock_guard<std::mutex> lock(g_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || ptr == nullptr) {
-      cudaGetLastError();
-      return ATF_ERR_CUDA;
-    }
-    g_scratch_ptr[dev] = static_cast<float*>(ptr);
+  int rc = load_driver_entry_points();
+  if (rc != ATF_OK) return rc;
+  unsigned long long id = 0;
+  if ((rc = current_ctx_id(&id)) != ATF_OK) return rc;
+  if (id != 0 && g_slot[dev].ctx_id == id && g_slot[dev].ptr != nullptr) {
+    *out = g_slot[dev].ptr;
+    return ATF_OK;
   }
-  *out = g_scratch_ptr[dev];
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || ptr == nullptr) {
+    cudaGetLastError();
+    return ATF_ERR_CUDA;
+  }
+  // the lookup made the runtime's context current if none was
+  if ((rc = current_ctx_id(&id)) != ATF_OK) return rc;
+  if (id == 0) return ATF_ERR_CUDA;
+  g_slot[dev].ctx_id = id;
+  g_slot[dev].ptr = static_cast<float*>(ptr);
+  *out = g_slot[dev].ptr;
   return ATF_OK;
 }
 

@@ -15,7 +15,7 @@
  *  - Kernels run on the caller's stream. The library keeps no mutable global
  *    state except the lazily loaded driver entry point used to encode TMA
  *    descriptors and, for atf_decode_run_noalloc only, its scratch array and
- *    the per-device address of that array.
+ *    the address of that array in each CUDA context.
  *  - head_dim is 128. GQA group sizes 1..16 (1/2/3/4/7/8 are the tested ones).
  *  - Device-side waits are bounded. A wait that expires writes a non-zero code
  *    to params->error_flag (if not NULL) and the kernel returns early; read it
@@ -156,7 +156,7 @@ typedef struct {
   const int32_t* indices;       /* device [nnz_pages] */
   const int32_t* last_page_len; /* device [B] */
   const int32_t* items;         /* device, from atf_decode_plan */
-  const int32_t* item_indptr;   /* device [B+1] */
+  const int32_t* item_indptr;   /* device [B+1], from atf_decode_plan (last entry = num_items) */
   int32_t num_items;
   int32_t batch_size, num_qo_heads, num_kv_heads, head_dim, page_size;
   const int64_t* q_pos;   /* optional device [B]: global position of the query (default kv_len-1) */
@@ -165,10 +165,11 @@ typedef struct {
   int window;                          /* ATF_WINDOW_OFF / SNAP16 / VEC8 */
   int32_t zhi16[ATF_MAX_LEVELS];       /* SNAP16: per-key 16-dim levels */
   int32_t zhi8[ATF_MAX_SLICES];        /* VEC8: per 8-dim slice (sorted-pair layout only) */
-  float* partial_o;   /* workspace [num_items, Hq, 128] fp32 */
+  float* partial_o;   /* workspace [num_items, Hq, 128] fp32, 16-byte aligned */
   float* partial_lse; /* workspace [num_items, Hq] fp32 (log2 domain) */
-  void* out;          /* [B, Hq, 128], bf16 or fp32 per out_dtype */
-  int64_t o_stride_b, o_stride_h;
+  void* out;          /* [B, Hq, 128], bf16 or fp32 per out_dtype; 8-byte aligned
+                         (16 for fp32) */
+  int64_t o_stride_b, o_stride_h; /* multiples of 4 elements */
   int out_dtype;      /* ATF_DTYPE_BF16 or ATF_DTYPE_F32 */
   float* lse_out;     /* optional fp32 [B, Hq], natural log */
   int* error_flag;
@@ -207,9 +208,12 @@ int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream);
  *    (on different streams with no ordering between them, or from several
  *    threads) race and corrupt each other's output. Issue them on one stream,
  *    or order them with events.
- *  - The first call on each device looks up the scratch address with
- *    cudaGetSymbolAddress. Make that first call before any stream capture
- *    begins on that device. */
+ *  - The first call in each CUDA context looks up the scratch address with
+ *    cudaGetSymbolAddress (a context is told apart by its cuCtxGetId, so a
+ *    device reset or a caller-made context gets its own lookup). Make that
+ *    first call before any stream capture begins in that context.
+ *  - item_indptr[batch_size] must equal num_items, as atf_decode_plan writes
+ *    it; the merge never reads a part at or past num_items. */
 #define ATF_NOALLOC_MAX_PARTIAL_ROWS 16384 /* 8 MiB + 64 KiB of fp32 scratch per device */
 int atf_decode_run_noalloc(const AtfDecodeParams* p, atf_stream_t stream);
 

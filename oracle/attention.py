@@ -108,7 +108,8 @@ def ref_window_attn(q, k, v, wvec, *, phase, block_m, block_n, mode="fp32",
             qm = min(block_m, M - q0)
             g0 = q0 + q_offset                       # global position of the tile's first row
             n_hi = min(g0 + qm, N) if phase == "prefill" else N
-            segs = WT.deff_segments(phase, g0, n_hi, block_m, block_n, N, wvec, d)
+            seg_fn = WT.deff_segments if n_hi <= 4096 * block_n else WT.deff_segments_bisect
+            segs = seg_fn(phase, g0, n_hi, block_m, block_n, N, wvec, d)
             for hk in range(hkv):
                 qt = q[bi, hk * G:(hk + 1) * G, q0:q0 + qm, :].astype(np.float32)  # (G, qm, d)
                 qt2 = qt.reshape(G * qm, d)

@@ -8,7 +8,8 @@ per-tile schedule:
   n_active            atflash/window_table.py:57-59, window_tables/atflash_window.py:71-74
   deff_of_zmin        atflash/window_table.py:62-67, window_tables/atflash_window.py:77-82
   zmin_tile           atflash/window_table.py:70-76
-  deff_segments       atflash/window_table.py:79-102
+  deff_segments       atflash/window_table.py:79-102 (deff_segments_bisect: the same
+                      runs by bisection, for long decode contexts)
   mma_slice_stats     atflash/window_table.py:105-128
   zhi_table           window_tables/atflash_window.py:85-108 (binary search per level)
   window_zhi_from_kret window_tables/atflash_window.py:111-116
@@ -75,6 +76,34 @@ def deff_segments(phase, q0, n_hi, block_m, block_n, n_ctx, wvec, head_dim):
             n1 += block_n
         segs.append((n0, min(n1, n_hi), deff))
         n0 = n1
+    return segs
+
+
+def deff_segments_bisect(phase, q0, n_hi, block_m, block_n, n_ctx, wvec, head_dim):
+    """The runs of deff_segments, found by bisection instead of a walk over every
+    key tile. z_min of a key tile falls as n0 grows (prefill and decode alike),
+    so D_eff is non-decreasing along the key axis and each run ends at the last
+    tile that still has the run's D_eff. Same output as deff_segments (checked
+    by tests/test_window_table.py); used for long decode contexts, where the
+    walk over one-key tiles would take seconds per call."""
+    nt = (n_hi + block_n - 1) // block_n
+
+    def f(t):
+        return deff_of_zmin(zmin_tile(phase, q0, t * block_n, block_m, block_n, n_ctx), wvec, head_dim)
+
+    segs = []
+    t = 0
+    while t < nt:
+        d = f(t)
+        lo, hi = t, nt - 1
+        while lo < hi:
+            mid = (lo + hi + 1) // 2
+            if f(mid) == d:
+                lo = mid
+            else:
+                hi = mid - 1
+        segs.append((t * block_n, min((lo + 1) * block_n, n_hi), d))
+        t = lo + 1
     return segs
 
 

@@ -3,6 +3,7 @@ ref_window_attn(phase="decode", block_m=1, block_n=1) for the 16-snap window
 (per-key levels) and ref_decode_sliced (gates/g2_correctness.py:43-70) for the
 vec8 window; window off == k=inf bitwise (gates/g1_bitexact.py analogue); split
 and KV-sharded runs merged by LSE equal the single run."""
+import json
 import math
 import os
 
@@ -156,32 +157,41 @@ def test_decode_vec8_matches_g2_oracle(cuda_device):
         assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
 
 
-def test_decode_against_golden(cuda_device):
-    """Kernel vs the reference's recorded decode outputs (contiguous KV as one-token pages)."""
-    import json
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "attn_cases.json")))
+
+
+@pytest.mark.parametrize("page", [1, 16])
+@pytest.mark.parametrize("case", GOLDEN["decode"], ids=lambda c: c["name"])
+def test_decode_against_golden(cuda_device, case, page):
+    """Kernel vs the reference's recorded decode outputs, window on (every
+    recorded k, 16-snap and vec8) and off. The contiguous KV is cut into pages
+    of 1 token (the cp.async kernel) or 16 tokens (the TMA kernel)."""
     from _inputs import make_bhsd
     import atflash
-    case = json.load(open(os.path.join(HERE, "golden", "attn_cases.json")))["decode"][0]
     gold = np.load(os.path.join(HERE, "golden", f"attn_{case['name']}.npz"))
     q, k, v, _ = make_bhsd(case["hq"], case["hkv"], case["N"], 128, case["base"], case["seed"], phase="decode")
     N, hkv = case["N"], case["hkv"]
-    kc = k[0].permute(1, 0, 2).reshape(N, 1, hkv, 128).contiguous()  # page_size 1, NHD
-    vc = v[0].permute(1, 0, 2).reshape(N, 1, hkv, 128).contiguous()
-    indptr = torch.tensor([0, N], dtype=torch.int32)
-    indices = torch.arange(N, dtype=torch.int32)
-    lpl = torch.tensor([1], dtype=torch.int32)
+    npg = (N + page - 1) // page
+    pad = npg * page - N
+    kt = torch.cat([k[0].permute(1, 0, 2), torch.zeros((pad, hkv, 128), dtype=k.dtype)])
+    vt = torch.cat([v[0].permute(1, 0, 2), torch.zeros((pad, hkv, 128), dtype=v.dtype)])
+    kc = kt.reshape(npg, page, hkv, 128).contiguous()  # NHD pages in order
+    vc = vt.reshape(npg, page, hkv, 128).contiguous()
+    indptr = torch.tensor([0, npg], dtype=torch.int32)
+    indices = torch.arange(npg, dtype=torch.int32)
+    lpl = torch.tensor([N - (npg - 1) * page], dtype=torch.int32)
     for kr in case["k_rets"]:
         tag = "inf" if kr == "inf" else f"{kr:g}"
         wt = None if kr == "inf" else atflash.WindowTable(128, case["base"], float(kr))
-        out = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, 1,
+        out = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, page,
                          "NHD", wt)
         mx, mean = err_stats(out[0].float().cpu().numpy(), gold[f"out32_k{tag}"][0, :, 0])
-        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (tag, mx, mean)
         if wt is not None:
-            out8 = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, 1,
+            out8 = run_decode(cuda_device, q[0, :, 0][None], kc, vc, indptr, indices, lpl, case["hq"], hkv, page,
                               "NHD", wt, window_mode="vec8")
             mx, mean = err_stats(out8[0].float().cpu().numpy(), gold[f"vec8_k{tag}"])
-            assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+            assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (tag, mx, mean)
 
 
 def test_decode_rotate_half_cache(cuda_device):

@@ -7,6 +7,7 @@ on and off; the reference's own relative rule (max <= 2*anchor + 2e-3,
 microbench/b1_correctness.py:89-91) is checked next to it. Bit-identity gates
 adapted from gates/g1_bitexact.py (window None == k=inf) and
 gates/c0_chunk_neutrality.py (chunked / sharded == single shot)."""
+import json
 import math
 import os
 
@@ -110,18 +111,24 @@ def test_prefill_batch_of_two(cuda_device):
         assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (b, mx, mean)
 
 
-@pytest.mark.parametrize("case", [(3, 1, 448, 1e4, 2.0, 777), (7, 1, 320, 1e4, 1.0, 778)],
-                         ids=["prefill_g3", "prefill_g7"])
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "attn_cases.json")))
+
+
+@pytest.mark.parametrize("case", GOLDEN["prefill"], ids=lambda c: c["name"])
 def test_prefill_against_golden(cuda_device, case):
-    """Kernel vs the reference's own recorded fp32 outputs (tests/golden)."""
-    hq, hkv, N, base, k_ret, seed = case
-    name = "prefill_g3" if hq == 3 else "prefill_g7"
-    gold = np.load(os.path.join(HERE, "golden", f"attn_{name}.npz"))
-    q, k, v, _ = make_bhsd(hq, hkv, N, 128, base, seed)
-    out = _run(q, k, v, cuda_device, base, k_ret).transpose(1, 2).float().cpu().numpy()
-    mx, mean = err_stats(out, gold[f"out32_k{k_ret:g}"])
-    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
-    assert mx <= 2 * float(gold[f"anchor_k{k_ret:g}"]) + 2e-3
+    """Kernel vs the reference's own recorded fp32 outputs (tests/golden), window
+    on (every recorded k) and off, at RoPE bases 1e4, 5e5 and 1e7."""
+    gold = np.load(os.path.join(HERE, "golden", f"attn_{case['name']}.npz"))
+    q, k, v, _ = make_bhsd(case["hq"], case["hkv"], case["N"], 128, case["base"], case["seed"])
+    rows = (np.concatenate([np.arange(t * 128, min((t + 1) * 128, case["N"])) for t in case["tiles"]])
+            if "tiles" in case else np.arange(case["N"]))
+    for kr in case["k_rets"]:
+        tag = "inf" if kr == "inf" else f"{kr:g}"
+        k_ret = float("inf") if kr == "inf" else float(kr)
+        out = _run(q, k, v, cuda_device, case["base"], k_ret).transpose(1, 2).float().cpu().numpy()[:, :, rows]
+        mx, mean = err_stats(out, gold[f"out32_k{tag}"])
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (tag, mx, mean)
+        assert mx <= 2 * float(gold[f"anchor_k{tag}"]) + 2e-3, (tag, mx)
 
 
 def test_prefill_pv_path_uniform_scores(cuda_device):

@@ -100,6 +100,35 @@ def test_invalid_arguments_rejected_without_gpu():
     assert lib.atf_rope_pack(ctypes.byref(r), None) == -1  # in place
 
 
+def test_decode_run_rejects_misaligned_workspace_and_output():
+    """The split kernel stores float4 rows into partial_o and the merge stores
+    4 values per lane into out; misaligned buffers or output strides are
+    refused before any launch."""
+    from atflash import _ffi
+    lib = _lib()
+
+    def params():
+        d = _ffi.AtfDecodeParams()
+        d.q = d.k_cache = d.v_cache = d.indptr = d.indices = d.last_page_len = 256
+        d.items = d.item_indptr = d.partial_o = d.partial_lse = d.out = 256
+        d.head_dim, d.batch_size, d.num_qo_heads, d.num_kv_heads, d.page_size = 128, 1, 8, 8, 16
+        d.kv_stride_page, d.kv_stride_token, d.kv_stride_head = 16 * 8 * 128, 8 * 128, 128
+        d.q_stride_b, d.q_stride_h = 8 * 128, 128
+        d.o_stride_b, d.o_stride_h = 8 * 128, 128
+        d.num_pages = 1
+        return d
+
+    for field, value in (("partial_o", 264), ("partial_lse", 258), ("out", 260), ("o_stride_b", 1026),
+                         ("o_stride_h", 130)):
+        d = params()
+        setattr(d, field, value)
+        assert lib.atf_decode_run(ctypes.byref(d), None) == -3, field
+    d = params()
+    d.out_dtype = _ffi.ATF_DTYPE_F32
+    d.out = 264  # 8-byte aligned is enough for bf16, not for fp32
+    assert lib.atf_decode_run(ctypes.byref(d), None) == -3
+
+
 def _plan(lib, lens, page, hq=24, hkv=8, **kw):
     from atflash import _ffi
     npages = [(n + page - 1) // page for n in lens]

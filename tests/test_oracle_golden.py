@@ -21,19 +21,29 @@ def _k(x):
     return float("inf") if x == "inf" else float(x)
 
 
+def golden_rows(case):
+    """Output rows a prefill fixture holds: all of them, or the rows of the
+    128-row query tiles listed under "tiles"."""
+    if "tiles" not in case:
+        return np.arange(case["N"])
+    return np.concatenate([np.arange(t * 128, min((t + 1) * 128, case["N"])) for t in case["tiles"]])
+
+
 @pytest.mark.parametrize("case", CASES["prefill"], ids=lambda c: c["name"])
 def test_oracle_prefill_matches_reference(case):
     q, k, v, _ = make_bhsd(case["hq"], case["hkv"], case["N"], case["d"], case["base"], case["seed"])
     assert sha_bf16(q) == case["sha_q"] and sha_bf16(k) == case["sha_k"] and sha_bf16(v) == case["sha_v"]
     gold = np.load(os.path.join(HERE, "golden", f"attn_{case['name']}.npz"))
+    rows = golden_rows(case)
     for kr in case["k_rets"]:
         tag = "inf" if kr == "inf" else f"{kr:g}"
         w = OWT.wavelengths_sorted(case["d"], case["base"], _k(kr))
+        kw = {"q_tiles": case["tiles"]} if "tiles" in case else {}
         o32 = OA.ref_window_attn(to_np(q), to_np(k), to_np(v), w, phase="prefill",
-                                 block_m=case["block_m"], block_n=case["block_n"], mode="fp32")
+                                 block_m=case["block_m"], block_n=case["block_n"], mode="fp32", **kw)[:, :, rows]
         np.testing.assert_allclose(o32, gold[f"out32_k{tag}"], rtol=0, atol=2e-5)
         o16 = OA.ref_window_attn(to_np(q), to_np(k), to_np(v), w, phase="prefill",
-                                 block_m=case["block_m"], block_n=case["block_n"], mode="bf16")
+                                 block_m=case["block_m"], block_n=case["block_n"], mode="bf16", **kw)[:, :, rows]
         anchor = float(np.abs(o16 - o32).max())
         # the bf16 anchor is an emulation; it must be of the reference's magnitude
         assert 0.25 * float(gold[f"anchor_k{tag}"]) <= anchor <= 4.0 * float(gold[f"anchor_k{tag}"])
@@ -68,6 +78,16 @@ def test_window_is_active_in_fixtures():
             w = OWT.wavelengths_sorted(case["d"], case["base"], _k(kr))
             st = OWT.mma_slice_stats("prefill", case["N"], case["N"], 128, 128, w, case["d"])
             assert st["qk_slice_ratio"] < 1.0
+            if "tiles" in case:  # the recorded tiles themselves cut levels
+                last = max(case["tiles"]) * 128
+                segs = OWT.deff_segments("prefill", last, last + 128, 128, 128, case["N"], w, case["d"])
+                assert min(dd for (_, _, dd) in segs) < case["d"]
+    for case in CASES["decode"]:
+        for kr in case["k_rets"]:
+            if kr == "inf":
+                continue
+            w = OWT.wavelengths_sorted(case["d"], case["base"], _k(kr))
+            assert OWT.deff_of_zmin(case["N"] - 1, w, case["d"]) < case["d"]
 
 
 def test_lse_merge_identity():

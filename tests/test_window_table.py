@@ -186,3 +186,16 @@ def test_pair_order_gate():
     assert not WT.pair_order_from_inv_freq(inv)[1]
     with pytest.raises(ValueError):
         WT.WindowTable.from_inv_freq(inv, 2.0)
+
+
+@pytest.mark.parametrize("base,k_ret", [(1e4, 2.0), (5e5, 2.0), (1e7, 64.0), (1e7, 2.0), (5e5, float("inf"))])
+def test_bisected_segments_equal_the_tile_walk(base, k_ret):
+    """deff_segments_bisect (used by the oracle for long decode contexts) gives
+    exactly the runs of the reference's tile-by-tile walk (deff_segments)."""
+    w = OWT.wavelengths_sorted(128, base, k_ret)
+    for (phase, q0, n_hi, bm, bn, n_ctx) in [("decode", 0, 20000, 1, 1, 20000), ("decode", 0, 4099, 1, 16, 4099),
+                                             ("prefill", 8192, 8192 + 128, 128, 128, 9000),
+                                             ("prefill", 3000, 3064, 64, 32, 3064), ("prefill", 0, 100, 128, 128, 100),
+                                             ("decode", 0, 1, 1, 1, 1)]:
+        assert OWT.deff_segments_bisect(phase, q0, n_hi, bm, bn, n_ctx, w, 128) == \
+            OWT.deff_segments(phase, q0, n_hi, bm, bn, n_ctx, w, 128)

@@ -102,6 +102,34 @@ def test_noalloc_equals_allocating_decode_on_two_calls_in_a_row():
 
 
 @pytest.mark.gpu
+def test_noalloc_fills_the_whole_scratch():
+    """A plan that uses every one of the ATF_NOALLOC_MAX_PARTIAL_ROWS rows (512
+    one-item requests x 32 heads): the last row lands at the end of the scratch
+    and the output still equals atf_decode_run bit for bit, on two calls."""
+    import atflash
+    from atflash import _runtime
+    dev = torch.device("cuda:0")
+    case = ([64 + (i % 7) for i in range(512)], 32, 8, 16, "NHD")
+    out_ref, lse_ref, p, _keep = _decode_with_params(dev, case, 11, atflash.WindowTable(128, 1e4, 2.0))
+    assert p.num_items * p.num_qo_heads == _ffi.ATF_NOALLOC_MAX_PARTIAL_ROWS
+    lib = _ffi.load()
+    p.partial_o = None
+    p.partial_lse = None
+    for _ in range(2):
+        out = torch.full_like(out_ref, float("nan"))
+        lse = torch.full_like(lse_ref, float("nan"))
+        p.out = out.data_ptr()
+        p.lse_out = lse.data_ptr()
+        with torch.cuda.device(dev):
+            rc = lib.atf_decode_run_noalloc(ctypes.byref(p), _runtime.stream_handle(dev))
+        _ffi.check("atf_decode_run_noalloc", rc)
+        torch.cuda.synchronize()
+        assert atflash.check_device_errors() == 0
+        assert torch.equal(out, out_ref)
+        assert torch.equal(lse, lse_ref)
+
+
+@pytest.mark.gpu
 def test_noalloc_rejects_an_oversized_plan_on_the_device():
     import atflash
     dev = torch.device("cuda:0")
