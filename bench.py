@@ -244,7 +244,18 @@ def timed(fn, steps, warmup, world, stream=None, sampler=None):
     if sampler:
         clocks = merge_clocks(clocks, world)
     ms = e0.elapsed_time(e1) / steps
-    return max_over_ranks(ms, world), clocks
+    timed.per_rank = all_ranks(ms, world)
+    return max(timed.per_rank), clocks
+
+
+def all_ranks(x, world):
+    """x of every rank, in rank order (a one-float all-gather)."""
+    if world == 1:
+        return [x]
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = torch.empty(world, dtype=torch.float64, device="cuda")
+    dist.all_gather_into_tensor(out, t)
+    return out.tolist()
 
 
 def prefill_inputs(device, copies=2, seed=2026):
@@ -258,55 +269,119 @@ def prefill_inputs(device, copies=2, seed=2026):
     return out
 
 
-def cpu_baseline_sample(n_tiles=20, heads=7, k_ret=K_RET):
-    """Time the numpy oracle on `n_tiles` query tiles x `heads` heads (one kv
-    group) of the config-2 workload; extrapolate to the full prefill by FLOPs."""
-    import numpy as np
-    from oracle import attention as OA
-    from oracle import window_table as OWT
+def _reference_cpu():
+    """The reference's own torch CPU path, byte-compiled into oracle/_ref by
+    oracle/build_ref.py (kind "reference"), or None when it was not built."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    try:
+        import build_ref
+    finally:
+        sys.path.pop(0)
+    return build_ref.load()
+
+
+def cpu_prefill_sample(n_sample=8192, k_ret=K_RET, threads=None):
+    """A bounded sample of the config-2 workload on the host cores: one kv-head
+    group (7 q heads over 1 kv head) of the 28/4-head windowed causal prefill at
+    n_sample keys, theta 1e7, window k, through the reference's own
+    ref_window_attn(mode="fp32") (atflash/reference.py:27-80) with all host
+    threads; the numpy restatement (oracle/attention.py) stands in when the
+    compiled reference is absent. Returns (sample ms, ms scaled to one full
+    131072-token 28-head prefill by windowed FLOPs, info)."""
     from atflash import window_table as WT
-    rng = np.random.default_rng(0)
-    w = OWT.wavelengths_sorted(D, THETA, k_ret)
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    G = HQ // HKV
+    g = torch.Generator(device="cpu").manual_seed(2026)
+    q = torch.randn((1, G, n_sample, D), generator=g).to(torch.bfloat16)
+    k = torch.randn((1, 1, n_sample, D), generator=g).to(torch.bfloat16)
+    v = torch.randn((1, 1, n_sample, D), generator=g).to(torch.bfloat16)
+    R = _reference_cpu()
+    if R is not None:
+        w = R.window_table.wavelengths_sorted(D, THETA, k_ret)
+        fn = lambda: R.reference.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128,
+                                                 mode="fp32")
+        kind, what = "reference", "atflash/reference.py ref_window_attn(mode='fp32') under torch (oracle/_ref)"
+    else:
+        from oracle import attention as OA
+        from oracle import window_table as OWT
+        w = OWT.wavelengths_sorted(D, THETA, k_ret)
+        qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
+        fn = lambda: OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=128, block_n=128)
+        kind, what = "port", "numpy restatement oracle/attention.py (the compiled reference was not built)"
+    t0 = time.perf_counter()
+    fn()
+    ms = (time.perf_counter() - t0) * 1e3
     zhi = WT.window_zhi_from_kret(D, THETA, k_ret, 2 ** 31 - 1)
-    total = WT.prefill_work(HQ, N_CTX, N_CTX, zhi)["flops"]
-    tiles = [int((i + 0.5) * (N_CTX // 128) / n_tiles) for i in range(n_tiles)]
-    sec = 0.0
-    flops = 0.0
-    for t in tiles:
-        hi = (t + 1) * 128
-        q = rng.standard_normal((1, heads, 128, D), dtype=np.float32)
-        k = rng.standard_normal((1, 1, hi, D), dtype=np.float32)
-        v = rng.standard_normal((1, 1, hi, D), dtype=np.float32)
-        t0 = time.perf_counter()
-        OA.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128, q_offset=t * 128)
-        sec += time.perf_counter() - t0
-        flops += WT.prefill_work(heads, 128, hi, zhi, q_offset=t * 128)["flops"]
-    ms_full = sec * (total / flops) * 1e3
-    return ms_full, {"cores": os.cpu_count(), "kind": "port",
-                     "sample": f"numpy oracle (oracle/attention.py) on query tiles {tiles} x {heads} heads "
-                               f"of the 131072-token config-2 prefill, extrapolated by windowed FLOPs "
-                               f"({flops:.3g} of {total:.3g}); {sec:.2f} s of CPU work"}
+    f_sample = WT.prefill_work(G, n_sample, n_sample, zhi)["flops"]
+    f_full = WT.prefill_work(HQ, N_CTX, N_CTX, zhi)["flops"]
+    info = {"cores": threads, "kind": kind,
+            "sample": f"{what}: {G} q heads / 1 kv head of the config-2 prefill (theta 1e7, k={k_ret:g}) at "
+                      f"{n_sample} tokens, {ms:.0f} ms measured; value = that time x {f_full / f_sample:.1f} "
+                      f"(windowed FLOPs of the full {N_CTX}-token 28-head prefill / of the sample)",
+            "sample_ms_measured": ms, "flops_sample": f_sample, "flops_full": f_full}
+    return ms, ms * f_full / f_sample, info
 
 
-def config1_cpu(k_rets=(2.0, float("inf"))):
-    """BASELINE config 1 on the host: the numpy oracle (ref_window_attn, fp32) at
-    batch 1, 24/8 heads, N=2048, theta 5e5, window k=2 and off, at the kernel's
-    tiling; ms per call (median of 3, all host threads)."""
-    import numpy as np
-    from oracle import attention as OA
-    from oracle import window_table as OWT
-    rng = np.random.default_rng(1)
-    f = lambda *sh: OA.bf16_round(rng.standard_normal(sh).astype(np.float32))
-    q, k, v = f(1, 24, 2048, 128), f(1, 8, 2048, 128), f(1, 8, 2048, 128)
-    res = {}
+def config1_cpu(k_rets=(2.0, float("inf")), reps=3):
+    """BASELINE config 1 in full on the host: the reference's ref_window_attn
+    (fp32, torch, all host threads; the numpy restatement when the compiled
+    reference is absent) at batch 1, 24/8 heads, N=2048, theta 5e5, window k=2
+    and off, at the kernel's 128 x 128 tiling; median ms of `reps` calls."""
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator(device="cpu").manual_seed(777)
+    q = torch.randn((1, 24, 2048, D), generator=g).to(torch.bfloat16)
+    k = torch.randn((1, 8, 2048, D), generator=g).to(torch.bfloat16)
+    v = torch.randn((1, 8, 2048, D), generator=g).to(torch.bfloat16)
+    R = _reference_cpu()
+    res = {"kind": "reference" if R is not None else "port", "threads": os.cpu_count()}
     for kr in k_rets:
-        w = OWT.wavelengths_sorted(128, 5e5, kr)
+        if R is not None:
+            w = R.window_table.wavelengths_sorted(D, 5e5, kr)
+            fn = lambda: R.reference.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128)
+        else:
+            from oracle import attention as OA
+            from oracle import window_table as OWT
+            w = OWT.wavelengths_sorted(D, 5e5, kr)
+            qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
+            fn = lambda: OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=128, block_n=128)
         ts = []
-        for _ in range(3):
+        for _ in range(reps):
             t0 = time.perf_counter()
-            OA.ref_window_attn(q, k, v, w, phase="prefill", block_m=128, block_n=128)
+            fn()
             ts.append((time.perf_counter() - t0) * 1e3)
-        res["on_k2" if kr == 2.0 else "off"] = statistics.median(ts)
+        res["on_k2_ms" if kr == 2.0 else "off_ms"] = statistics.median(ts)
+    return res
+
+
+def decode8k_cpu(k_rets=(2.0, float("inf"))):
+    """BASELINE config 3 at 8K keys in full on the host: 8 requests x 24/8 heads,
+    theta 5e5, through the reference's ref_window_attn(phase="decode",
+    block_m=1, block_n=1) per request (the reference is not paged; the page
+    table only permutes storage). ms per decode step (all 8 requests)."""
+    torch.set_num_threads(os.cpu_count())
+    B, hq, hkv, N = 8, 24, 8, 8192
+    g = torch.Generator(device="cpu").manual_seed(1234 + N + D)
+    q = torch.randn((B, hq, 1, D), generator=g).to(torch.bfloat16)
+    k = torch.randn((B, hkv, N, D), generator=g).to(torch.bfloat16)
+    v = torch.randn((B, hkv, N, D), generator=g).to(torch.bfloat16)
+    R = _reference_cpu()
+    res = {"kind": "reference" if R is not None else "port", "threads": os.cpu_count()}
+    for kr in k_rets:
+        if R is not None:
+            w = R.window_table.wavelengths_sorted(D, 5e5, kr)
+            fn = lambda b: R.reference.ref_window_attn(q[b:b + 1], k[b:b + 1], v[b:b + 1], w, phase="decode",
+                                                       block_m=1, block_n=1)
+        else:
+            from oracle import attention as OA
+            from oracle import window_table as OWT
+            w = OWT.wavelengths_sorted(D, 5e5, kr)
+            fn = lambda b: OA.ref_window_attn(q[b:b + 1].float().numpy(), k[b:b + 1].float().numpy(),
+                                              v[b:b + 1].float().numpy(), w, phase="decode", block_m=1, block_n=1)
+        t0 = time.perf_counter()
+        for b in range(B):
+            fn(b)
+        res["on_k2_ms" if kr == 2.0 else "off_ms"] = (time.perf_counter() - t0) * 1e3
     return res
 
 
@@ -325,24 +400,123 @@ def config1_gpu(device):
 
 
 def run_reference(args, rank, world):
+    """--impl reference: the reference's own CPU path on this box's host cores,
+    rank 0 only. Each step is the bounded config-2 sample of cpu_prefill_sample;
+    `value` is the median step scaled to one full config-2 prefill by windowed
+    FLOPs (the full prefill would take about a quarter of an hour on the CPU).
+    Config 1 and the config-3 8K decode, which the CPU finishes in seconds, are
+    measured in full beside it."""
     if rank != 0:
         return
-    samples = []
+    scaled, measured = [], []
     info = None
     for i in range(args.warmup + args.steps):
-        ms, info = cpu_baseline_sample(n_tiles=2, heads=7)
+        ms, full, info = cpu_prefill_sample()
         if i >= args.warmup:
-            samples.append(ms)
-    v = statistics.median(samples)
+            scaled.append(full)
+            measured.append(ms)
+    v = statistics.median(scaled)
+    info = dict(info, sample_ms_measured=statistics.median(measured))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "ms", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
             "config": {"workload": "prefill N=131072 Hq=28 Hkv=4 d=128 theta=1e7 k=2 (BASELINE config 2)",
                        "batch": 1, "seq_len": N_CTX},
+            "value_is": "a measured bounded sample of the workload, scaled by windowed FLOPs to one full prefill",
             "cpu_baseline": dict(info, value=v, unit="ms"),
             "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "config1_cpu_ms": config1_cpu()}
+            "config1_cpu_ms": config1_cpu(), "decode_8k_cpu_ms": decode8k_cpu()}
     print(json.dumps(line), flush=True)
+
+
+def cudnn_dense_ms(inputs, steps, warmup):
+    """The vendor's dense causal attention on the same config-2 inputs, for
+    comparison: torch scaled_dot_product_attention restricted to the cuDNN
+    backend (GQA 28/4, bf16, no window); ms per call, or the error text."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    def fn(i):
+        q, k, v = inputs[i % len(inputs)]
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                                             v.transpose(1, 2), is_causal=True, enable_gqa=True)
+    try:
+        ms, _ = timed(fn, steps, warmup, 1)
+        return ms
+    except Exception:
+        pass
+    # cuDNN without the GQA flag: the kv heads expanded to the 28 q heads first
+    # (outside the timed region)
+    expanded = [(q, k.repeat_interleave(HQ // HKV, dim=2), v.repeat_interleave(HQ // HKV, dim=2))
+                for (q, k, v) in inputs]
+
+    def fn2(i):
+        q, k, v = expanded[i % len(expanded)]
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                                             v.transpose(1, 2), is_causal=True)
+    try:
+        ms, _ = timed(fn2, steps, warmup, 1)
+        return ms
+    except Exception as e:  # backend refused the shape: report why
+        return f"unavailable: {type(e).__name__}: {str(e)[:200]}"
+    finally:
+        del expanded
+
+
+def _err_stats(out, ref):
+    """max and mean abs error over the finite reference entries."""
+    import numpy as np
+    m = np.isfinite(ref)
+    d = np.abs(out.astype(np.float64)[m] - ref.astype(np.float64)[m])
+    return float(d.max()), float(d.mean())
+
+
+def all_ok(ok, world):
+    """True on every rank when `ok` holds on every rank."""
+    if world == 1:
+        return bool(ok)
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def prefill_parity(atflash, qkv, out, blocks, wt, rank, world):
+    """Correctness of the timed prefill, checked inside the bench run.
+
+    Every rank compares every row of the last 128-row query tile of its far
+    zig-zag block, for one q head, with the numpy oracle (ref_window_attn,
+    atflash/reference.py:27-80, all keys of the tile's causal range). With more
+    than one rank, each rank also runs the whole prefill on its own GPU and
+    checks that its blocks' rows are bit-identical to that single run."""
+    from oracle import attention as OA
+    from oracle import window_table as OWT
+    q, k, v = qkv
+    s, e = blocks[-1]
+    t0 = max(s, e - 128)
+    h = (3 * rank + 5) % HQ
+    hk = h // (HQ // HKV)
+    w = OWT.wavelengths_sorted(D, THETA, K_RET)
+    ref = OA.ref_window_attn(q[:, t0:e, h:h + 1].transpose(1, 2).float().cpu().numpy(),
+                             k[:, :e, hk:hk + 1].transpose(1, 2).float().cpu().numpy(),
+                             v[:, :e, hk:hk + 1].transpose(1, 2).float().cpu().numpy(), w, phase="prefill",
+                             block_m=128, block_n=128, q_offset=t0)
+    got = out[:, t0:e, h:h + 1].transpose(1, 2).float().cpu().numpy()
+    mx, mean = _err_stats(got, ref)
+    ok_oracle = mx <= 2e-2 and mean <= 2e-3
+    res = {"oracle_rows": [t0, e], "oracle_head": h, "oracle_max_abs": mx, "oracle_mean_abs": mean,
+           "tolerance": "max abs <= 2e-2, mean abs <= 2e-3 vs the fp32 oracle"}
+    ok = ok_oracle
+    if world > 1:
+        full = atflash.prefill_fwd(q, k, v, causal=True, window_table=wt)
+        torch.cuda.synchronize()
+        same = all(torch.equal(out[:, bs:be].view(torch.int16), full[:, bs:be].view(torch.int16))
+                   for (bs, be) in blocks if be > bs)
+        res["zigzag_rows_bit_equal_single_gpu_run"] = all_ok(same, world)
+        ok = ok and same
+        del full
+    res["ok"] = all_ok(ok, world)
+    return res
 
 
 def bench_decode(device, steps, warmup, peaks, N=131072):
@@ -430,12 +604,82 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
         res[name]["us_graph"] = ms_g * 1e3
         res[name]["gbs_aggregate_graph"] = total / (ms_g * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
+    res["parity"] = decode_1m_parity(device, rank, world, q, (kc, vc), perm, q_pos, kv_pos0, N, shard, page)
     res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, KV split into {world} shards, "
                      "all-gather of (O, LSE) + LSE merge inside the step; us: eager "
                      "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep")
     del kc, vc
     torch.cuda.empty_cache()
     return res
+
+
+def _decode_1m_shard(device, r, shard, page, hkv):
+    """Shard r of the config-5 KV cache, generated exactly as rank r generates it."""
+    npg = shard // page
+    g = torch.Generator(device="cpu").manual_seed(4242 + r)
+    perm = torch.randperm(npg, generator=g).to(torch.int32)
+    gd = torch.Generator(device=device).manual_seed(77 + r)
+    kc = torch.randn((npg, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    vc = torch.randn((npg, page, hkv, D), generator=gd, device=device).to(torch.bfloat16)
+    return kc, vc, perm
+
+
+def decode_1m_parity(device, rank, world, q, cache, perm, q_pos, kv_pos0, N, shard, page):
+    """Correctness of the config-5 step, checked inside the bench run, window
+    k=64 and off. One rank: q heads 0-6 (kv head 0) against the numpy oracle
+    (ref_window_attn phase="decode", every key). Several ranks: rank 0 decodes
+    every rank's shard on its own GPU (the shards regenerated from the ranks'
+    seeds), merges the partial states with the same LSE merge, and checks that
+    the sharded step's result is bit-identical to this single-GPU emulation."""
+    import atflash
+    hq, hkv = q.shape[1], cache[0].shape[2]
+    G = hq // hkv
+    out = {}
+    ok = True
+    for name, wt in (("on_k64", atflash.WindowTable(D, THETA, 64.0)), ("off", None)):
+        ws = torch.empty(64 * 1024 * 1024, dtype=torch.uint8, device=device)
+        w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        w.plan(torch.tensor([0, shard // page], dtype=torch.int32), perm, torch.tensor([page], dtype=torch.int32),
+               hq, hkv, D, page, window_table=wt)
+        o, l = atflash.dist.sharded_decode(q, w, cache, q_pos=q_pos, kv_pos0=kv_pos0)
+        torch.cuda.synchronize()
+        if rank == 0 and world == 1:
+            from oracle import attention as OA
+            from oracle import window_table as OWT
+            kc, vc = cache
+            pages = perm.to(device).long()
+            kk = kc[pages, :, 0].reshape(-1, D).float().cpu().numpy()
+            vv = vc[pages, :, 0].reshape(-1, D).float().cpu().numpy()
+            wv = OWT.wavelengths_sorted(D, THETA, 64.0 if wt is not None else float("inf"))
+            ref = OA.ref_window_attn(q[0, :G].float().cpu().numpy()[None, :, None, :], kk[None, None],
+                                     vv[None, None], wv, phase="decode", block_m=1, block_n=1)[0, :, 0]
+            mx, mean = _err_stats(o[0, :G].float().cpu().numpy(), ref)
+            good = mx <= 2e-2 and mean <= 2e-3
+            out[name] = {"oracle_max_abs": mx, "oracle_mean_abs": mean, "heads": f"q 0-{G - 1}"}
+        elif rank == 0:
+            po, pl = [], []
+            for r in range(world):
+                kc_r, vc_r, perm_r = (cache[0], cache[1], perm) if r == 0 else _decode_1m_shard(
+                    device, r, shard, page, hkv)
+                w_r = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+                w_r.plan(torch.tensor([0, shard // page], dtype=torch.int32), perm_r,
+                         torch.tensor([page], dtype=torch.int32), hq, hkv, D, page, window_table=wt)
+                o_r, l_r = w_r.run(q, (kc_r, vc_r), q_pos=q_pos,
+                                   kv_pos0=torch.tensor([r * shard], dtype=torch.int64, device=device),
+                                   return_lse=True, out_dtype=torch.float32)
+                po.append(o_r)
+                pl.append(l_r)
+                del kc_r, vc_r
+            eo, el = atflash.lse_merge(torch.stack(po), torch.stack(pl), lse_log2=False, out_dtype=o.dtype,
+                                       return_lse=True)
+            torch.cuda.synchronize()
+            good = torch.equal(eo.view(torch.int16), o.view(torch.int16)) and torch.equal(el, l)
+            out[name] = {"bit_equal_single_gpu_emulation": good}
+        else:
+            good = True
+        ok = ok and good
+    out["ok"] = all_ok(ok, world)
+    return out
 
 
 def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
@@ -523,7 +767,10 @@ def main():
 
     sampler = ClockSampler(local)
     ms_on, clocks = timed(step(wt2), args.steps, args.warmup, world, sampler=sampler)
+    per_rank_ms = timed.per_rank
     err = atflash.check_device_errors()
+    # `out` holds the last timed step's rows, computed from inputs[(steps - 1) % 2]
+    parity = prefill_parity(atflash, inputs[(args.steps - 1) % len(inputs)], out, blocks, wt2, rank, world)
     work_on = WT.prefill_work(HQ, N_CTX, N_CTX, wt2.zhi16)
     # per-rank work for the roofline of this rank's launches
     my_flops = sum(WT.prefill_work(HQ, e - s, e, wt2.zhi16, q_offset=s)["flops"] for (s, e) in blocks if e > s)
@@ -535,6 +782,8 @@ def main():
         work_64 = WT.prefill_work(HQ, N_CTX, N_CTX, wt64.zhi16)
         extras["prefill"] = {
             "k2_ms": ms_on, "off_ms": ms_off, "k64_ms": ms_64,
+            "k2_ms_per_rank": per_rank_ms,
+            "k2_imbalance_max_over_mean": max(per_rank_ms) / (sum(per_rank_ms) / len(per_rank_ms)),
             "ratio_on_off_k2": ms_off / ms_on, "ceiling_k2": work_on["ceiling"], "s_k2": work_on["s"],
             "ceiling_recovery_k2": (ms_off / ms_on - 1) / (work_on["ceiling"] - 1),
             "ratio_on_off_k64": ms_off / ms_64, "ceiling_k64": work_64["ceiling"],
@@ -542,6 +791,14 @@ def main():
             "tflops_off": work_on["flops_dense"] / (ms_off * 1e-3) / 1e12,
             "tflops_k64_algorithmic": work_64["flops"] / (ms_64 * 1e-3) / 1e12,
         }
+        if world == 1:
+            extras["prefill"]["cudnn_dense_sdpa_ms"] = cudnn_dense_ms(inputs, args.steps, args.warmup)
+        else:
+            # the optional all-gather of the output rows (every rank ends with the
+            # whole output), timed on its own after the prefill
+            outs = [(s, e, out[:, s:e]) for (s, e) in blocks]
+            ms_g, _ = timed(lambda i: atflash.dist.gather_zigzag(outs, N_CTX, world), args.steps, 3, world)
+            extras["prefill"]["gather_zigzag_ms"] = ms_g
     # e2e through the public API with host buffers: H2D of this rank's q rows and
     # of k/v, the prefill, D2H of this rank's output rows. The copies are
     # pipelined with the compute. A chunk of query rows [c0, c1) needs keys
@@ -625,10 +882,9 @@ def main():
     cpu = None
     config1 = None
     if not args.no_extras and rank == 0 and world == 1 and args.only == "all":
-        cms, info = cpu_baseline_sample()
+        _, cms, info = cpu_prefill_sample()
         cpu = dict(info, value=cms, unit="ms")
-        config1 = {"gpu_ms": config1_gpu(device), "cpu_oracle_ms": config1_cpu(),
-                   "cpu_cores": os.cpu_count(),
+        config1 = {"gpu_ms": config1_gpu(device), "cpu_ms": config1_cpu(),
                    "shape": "prefill batch 1, 24/8 heads, N=2048, d=128, theta 5e5 (BASELINE config 1)"}
     if rank == 0:
         achieved = my_flops / (ms_on * 1e-3) / 1e12
@@ -648,7 +904,10 @@ def main():
                            "l2": "inputs 1.2 GB per copy > 126 MB L2; two copies rotated"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
-                "device_error_flag": err, "extras": dict(extras, decode=decode, decode_1m_sharded=decode_1m, prefill_512k=prefill_512k,
+                "device_error_flag": err,
+                "parity_ok": bool(parity["ok"] and (decode_1m is None or decode_1m["parity"]["ok"])),
+                "parity": {"prefill": parity, "decode_1m": decode_1m["parity"] if decode_1m else None},
+                "extras": dict(extras, decode=decode, decode_1m_sharded=decode_1m, prefill_512k=prefill_512k,
                                 config1=config1)
                 if extras else None}
         print(json.dumps(line), flush=True)
