@@ -18,26 +18,77 @@ the build's sharding of the same computation.
 """
 from typing import Callable, List, Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
 TILE = 128
 
 
-def zigzag_bounds(seqlen: int, world: int, align: int = TILE) -> List[int]:
-    """2*world+1 block boundaries, interior ones on multiples of `align`."""
+def zigzag_bounds(seqlen: int, world: int, align: int = TILE, zhi: Optional[Sequence[int]] = None) -> List[int]:
+    """2*world+1 block boundaries, interior ones on multiples of `align`.
+
+    Without a window table the blocks have equal rows: under a causal mask the
+    work of a block grows linearly with its position, so blocks i and
+    2*world-1-i always add up to the same work. With a window (`zhi`, the
+    16-snap levels) a far key tile costs less than a near one and the work of a
+    row grows more slowly than its length, so equal rows would leave the ranks
+    holding the first blocks with the most work. Then the first half of the
+    sequence keeps equal-row blocks and the second half is cut so that every
+    rank's pair of blocks carries the same work, in the windowed FLOP model of
+    the kernel: a (query tile, key tile) step costs D_eff + head_dim."""
     nb = 2 * world
-    b = [0]
+    equal = [0]
     for i in range(1, nb):
         x = int(round(i * seqlen / nb / align)) * align
-        b.append(min(max(x, b[-1]), seqlen))
-    b.append(seqlen)
-    return b
+        equal.append(min(max(x, equal[-1]), seqlen))
+    equal.append(seqlen)
+    if zhi is None or world == 1:
+        return equal
+    cum = _cumulative_tile_work(seqlen, zhi, align)  # cum[t]: work of rows [0, t * align)
+    nt = len(cum) - 1
+    half = int(round(nt / 2))
+    b = [0] + [int(round(i * half / world)) for i in range(1, world)] + [half]
+    target = cum[nt] / world
+    tail = [nt]
+    for r in range(world - 1):  # rank r's far block ends where rank r-1's starts
+        want = target - (cum[b[r + 1]] - cum[b[r]])
+        lo_val = cum[tail[-1]] - want
+        t = int(np.searchsorted(cum, lo_val))
+        if t > 0 and abs(cum[t - 1] - lo_val) < abs(cum[t] - lo_val):
+            t -= 1
+        tail.append(min(max(t, half), tail[-1]))
+    tail.append(half)
+    b = [min(x * align, seqlen) for x in b[:-1] + tail[::-1]]
+    # the cuts sit on whole tiles, so keep whichever split is closer to even
+    return b if _max_pair_work(b, cum, world, align) < _max_pair_work(equal, cum, world, align) else equal
 
 
-def zigzag_blocks(seqlen: int, world: int, rank: int, align: int = TILE) -> List[Tuple[int, int]]:
-    """The two [start, end) query blocks of `rank`: blocks rank and 2*world-1-rank."""
-    b = zigzag_bounds(seqlen, world, align)
+def _max_pair_work(b, cum, world, align):
+    t = [(x + align - 1) // align for x in b]
+    return max((cum[t[r + 1]] - cum[t[r]]) + (cum[t[2 * world - r]] - cum[t[2 * world - 1 - r]])
+               for r in range(world))
+
+
+def _cumulative_tile_work(seqlen: int, zhi: Sequence[int], tile: int = TILE, head_dim: int = 128):
+    """Windowed work of the rows [0, t * tile) for every t (causal prefill, one head)."""
+    levels = np.asarray(list(zhi), dtype=np.int64)
+    nt = (seqlen + tile - 1) // tile
+    work = np.zeros(nt + 1, dtype=np.float64)
+    n0 = np.arange(nt, dtype=np.int64) * tile
+    for t in range(nt):
+        q0 = t * tile
+        z = np.maximum(0, q0 - (n0[:t + 1] + tile - 1))
+        L = np.maximum(1, (levels[None, :] >= z[:, None]).sum(axis=1))
+        work[t + 1] = work[t] + float((16 * L + head_dim).sum())
+    return work
+
+
+def zigzag_blocks(seqlen: int, world: int, rank: int, align: int = TILE,
+                  zhi: Optional[Sequence[int]] = None) -> List[Tuple[int, int]]:
+    """The two [start, end) query blocks of `rank`: blocks rank and 2*world-1-rank
+    (of zigzag_bounds, balanced for the window when `zhi` is given)."""
+    b = zigzag_bounds(seqlen, world, align, zhi)
     i, j = rank, 2 * world - 1 - rank
     return [(b[i], b[i + 1]), (b[j], b[j + 1])]
 
@@ -77,8 +128,9 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=
     S = q.shape[1]
     if k.shape[1] != S:
         raise ValueError("sharded prefill expects seqlen_q == seqlen_k")
+    zhi = getattr(window_table, "zhi16", None) if causal else None
     outs = []
-    for (s, e) in zigzag_blocks(S, world, rank):
+    for (s, e) in zigzag_blocks(S, world, rank, zhi=zhi):
         if e <= s:
             outs.append((s, e, q.new_empty((q.shape[0], 0, q.shape[2], q.shape[3]))))
             continue
@@ -88,12 +140,13 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=
         outs.append((s, e, o))
     if not gather:
         return outs
-    return gather_zigzag(outs, S, world, group)
+    return gather_zigzag(outs, S, world, group, zhi=zhi)
 
 
-def gather_zigzag(outs, seqlen: int, world: int, group=None) -> torch.Tensor:
-    """All-gather every rank's two blocks into the full output (rows in order)."""
-    bounds = zigzag_bounds(seqlen, world)
+def gather_zigzag(outs, seqlen: int, world: int, group=None, zhi: Optional[Sequence[int]] = None) -> torch.Tensor:
+    """All-gather every rank's two blocks into the full output (rows in order).
+    `zhi` must be the window levels the blocks were cut with (None: equal rows)."""
+    bounds = zigzag_bounds(seqlen, world, zhi=zhi)
     maxlen = max(bounds[i + 1] - bounds[i] for i in range(2 * world))
     ref = outs[0][2]
     B, _, H, D = ref.shape
@@ -104,7 +157,7 @@ def gather_zigzag(outs, seqlen: int, world: int, group=None) -> torch.Tensor:
     dist.all_gather_into_tensor(recv.view(-1), send.view(-1), group=group)
     full = ref.new_empty((B, seqlen, H, D))
     for r in range(world):
-        for t, (s, e) in enumerate(zigzag_blocks(seqlen, world, r)):
+        for t, (s, e) in enumerate(zigzag_blocks(seqlen, world, r, zhi=zhi)):
             full[:, s:e] = recv[r, t, :, : e - s]
     return full
 

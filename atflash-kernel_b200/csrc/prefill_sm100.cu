@@ -110,6 +110,12 @@ __device__ __forceinline__ void qk_group_asm(uint32_t d_tmem, uint64_t qd, uint6
       ::"r"(d_tmem), "l"(qd), "l"(kd), "r"(idesc), "r"(L), "r"(bar_addr)
       : "memory");
 }
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
 constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
 constexpr uint32_t QHALF_BYTES = BM * 16;             // 2 KB
@@ -452,14 +458,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           if ((a.causal && key > qpos) || key >= a.Sk) s[c] = -INFINITY;
         }
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+      // three-input max: 64 instructions for the 128 scores, 4 chains
+      float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+      float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-      for (int c = 4; c < BN; c += 4) {
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
-        mx2 = fmaxf(mx2, s[c + 2]);
-        mx3 = fmaxf(mx3, s[c + 3]);
+      for (int c = 12; c < BN - 8; c += 8) {
+        mx0 = fmax3(mx0, s[c], s[c + 1]);
+        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
       }
+      mx0 = fmax3(mx0, s[BN - 4], s[BN - 3]);
+      mx1 = fmax3(mx1, s[BN - 2], s[BN - 1]);
       const float mnew = fmaxf(m2, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
       // Lazy rescale: the running max only moves when it grows by more than
       // 8 (log2 units), so P <= 2^8 stays exact enough in bf16 and O is
@@ -477,17 +487,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       const float msub = (m2 == -INFINITY) ? 0.f : m2;
-      float ls0 = 0.f, ls1 = 0.f;
+      // exponentials, the row sum and the bf16 packing of P, two columns at a
+      // time with packed f32x2 arithmetic (half the FMA / add instructions)
       uint32_t pk[BN / 2];
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+      const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
 #pragma unroll
       for (int c = 0; c < BN / 2; ++c) {
-        const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -msub));
-        const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
-        ls0 += p0;
-        ls1 += p1;
-        pk[c] = pack_bf16x2(p0, p1);
+        const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sl2x2, negm);
+        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        if (c & 1) ls1 = __fadd2_rn(ls1, p); else ls0 = __fadd2_rn(ls0, p);
+        pk[c] = pack_bf16x2(p.x, p.y);
       }
-      l += ls0 + ls1;
+      {
+        const float2 ls = __fadd2_rn(ls0, ls1);
+        l += ls.x + ls.y;
+      }
       tmem_st64(tS, pk);
       if (__any_sync(FULL, need)) {
         // O holds the sum up to tile j-1 once PV(t, j-1) has completed (S_t(j) was

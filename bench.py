@@ -693,7 +693,7 @@ def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
     v = torch.randn((1, N, HKV, D), generator=g, device=device).to(torch.bfloat16)
     out = torch.empty_like(q)
     wt = atflash.WindowTable(D, THETA, K_RET)
-    blocks = atflash.dist.zigzag_blocks(N, world, rank) if world > 1 else [(0, N)]
+    blocks = atflash.dist.zigzag_blocks(N, world, rank, zhi=wt.zhi16) if world > 1 else [(0, N)]
 
     def fn(i):
         for (s0, e0) in blocks:
@@ -752,7 +752,7 @@ def main():
         return
     inputs = prefill_inputs(device)
     wt2 = atflash.WindowTable(D, THETA, K_RET)
-    blocks = atflash.dist.zigzag_blocks(N_CTX, world, rank) if world > 1 else [(0, N_CTX)]
+    blocks = atflash.dist.zigzag_blocks(N_CTX, world, rank, zhi=wt2.zhi16) if world > 1 else [(0, N_CTX)]
     out = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16, device=device)
     launches_per_step = len([b for b in blocks if b[1] > b[0]])
 
@@ -797,7 +797,8 @@ def main():
             # the optional all-gather of the output rows (every rank ends with the
             # whole output), timed on its own after the prefill
             outs = [(s, e, out[:, s:e]) for (s, e) in blocks]
-            ms_g, _ = timed(lambda i: atflash.dist.gather_zigzag(outs, N_CTX, world), args.steps, 3, world)
+            ms_g, _ = timed(lambda i: atflash.dist.gather_zigzag(outs, N_CTX, world, zhi=wt2.zhi16), args.steps,
+                            3, world)
             extras["prefill"]["gather_zigzag_ms"] = ms_g
     # e2e through the public API with host buffers: H2D of this rank's q rows and
     # of k/v, the prefill, D2H of this rank's output rows. The copies are

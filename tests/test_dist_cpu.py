@@ -32,6 +32,28 @@ def test_zigzag_partition_covers_and_balances():
                 assert max(work) - min(work) <= 0.02 * max(work), (N, world, work)
 
 
+@pytest.mark.parametrize("N", [131072, 524288, 4096 + 384])
+def test_windowed_zigzag_split_covers_and_is_not_less_even(N):
+    """With a window table the blocks are cut by windowed work (the kernel's
+    tile schedule); every row is covered once, every cut sits on the 128-row
+    tile grid, and the largest rank's work is never above the equal-row split's."""
+    from atflash import window_table as WT
+    zhi = WT.WindowTable(128, 1e7, 2.0).zhi16
+    cum = AD._cumulative_tile_work(N, zhi)
+    for world in (2, 4, 8):
+        seen = np.zeros(N, dtype=np.int32)
+        for r in range(world):
+            for (s, e) in AD.zigzag_blocks(N, world, r, zhi=zhi):
+                assert s % 128 == 0 and (e % 128 == 0 or e == N)
+                seen[s:e] += 1
+        assert (seen == 1).all()
+        bal = AD._max_pair_work(AD.zigzag_bounds(N, world, zhi=zhi), cum, world, 128)
+        eq = AD._max_pair_work(AD.zigzag_bounds(N, world), cum, world, 128)
+        assert bal <= eq
+    if N == 524288:  # far from even with equal rows at 512K, close to even after the cut
+        assert AD._max_pair_work(AD.zigzag_bounds(N, 8, zhi=zhi), cum, 8, 128) <= 1.003 * cum[-1] / 8
+
+
 def test_kv_shard_ranges():
     for N in (1048576, 1000, 77):
         for world in (1, 2, 4, 8):
