@@ -876,7 +876,6 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
     return ATF_ERR_INVALID_ARG;
   if (p->head_dim != ATF_HEAD_DIM) return ATF_ERR_UNSUPPORTED;
   if (p->num_qo_heads / p->num_kv_heads > 16) return ATF_ERR_UNSUPPORTED;
-  long long total = 0, maxlen = 0;
   for (int b = 0; b < p->batch_size; ++b) {
     const int np = p->indptr_host[b + 1] - p->indptr_host[b];
     const int lpl = p->last_page_len_host[b];
@@ -884,8 +883,6 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
     if (np > 0 && (lpl < 1 || lpl > p->page_size)) return ATF_ERR_INVALID_ARG;
     const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + lpl : 0;
     if (len > (1ll << 31) - 1) return ATF_ERR_UNSUPPORTED;
-    total += len;
-    maxlen = len > maxlen ? len : maxlen;
   }
   int sms = p->num_sms;
   if (sms <= 0) {
@@ -894,17 +891,40 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  // Aim for ~16 CTAs per SM in total (2 resident per SM -> ~8 waves, so the
-  // last wave's tail is small), in 64-key multiples, never below min_chunk
-  // keys and never above 16384 keys (the page list of an item is staged in
-  // shared memory by the TMA kernel).
-  const long long target_ctas = 16ll * sms;
+  // Item size. Every CTA (item, kv head) pays a fixed start-up and drain
+  // cost (barrier set-up, page list, the first loads' latency, the partial
+  // state write), so items are made as long as the occupancy allows: the
+  // CTAs are kept within the fewest full waves of 2 resident CTAs per SM
+  // that the longest allowed item (16384 keys, the page list staged in shared
+  // memory) permits, and within that the items are cut as finely as the waves
+  // hold (the most even split). Keys are cut in multiples of 64 (a stage).
+  const long long slots = 2ll * sms;
   const long long min_chunk = p->min_chunk_keys > 0 ? p->min_chunk_keys : 256;
-  long long chunk = (total * p->num_kv_heads + target_ctas - 1) / target_ctas;
-  if (chunk < min_chunk) chunk = min_chunk;
-  if (p->max_chunk_keys > 0 && chunk > p->max_chunk_keys) chunk = p->max_chunk_keys;
-  if (chunk > decode_tma::MAX_ITEM_KEYS) chunk = decode_tma::MAX_ITEM_KEYS;
-  chunk = (chunk + 63) / 64 * 64;
+  long long cap = decode_tma::MAX_ITEM_KEYS;
+  if (p->max_chunk_keys > 0 && p->max_chunk_keys < cap) cap = p->max_chunk_keys;
+  cap = cap / 64 * 64;
+  if (cap < 64) cap = 64;
+  auto ctas_for = [&](long long c) {
+    long long n = 0;
+    for (int b = 0; b < p->batch_size; ++b) {
+      const int np = p->indptr_host[b + 1] - p->indptr_host[b];
+      const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + p->last_page_len_host[b] : 0;
+      n += (len + c - 1) / c;
+    }
+    return n * p->num_kv_heads;
+  };
+  const long long waves = (ctas_for(cap) + slots - 1) / slots;
+  long long chunk = cap;
+  // the smallest chunk (most CTAs) that still fits in `waves` full waves
+  long long lo = (min_chunk + 63) / 64 * 64, hi = cap;
+  if (lo > hi) lo = hi;
+  while (lo < hi) {
+    const long long mid = (lo + hi) / 2 / 64 * 64;
+    if (mid < lo) break;
+    if (ctas_for(mid) <= waves * slots) hi = mid; else lo = mid + 64;
+  }
+  // the smallest such chunk also splits each request most evenly
+  chunk = hi;
   if (chunk < 64) chunk = 64;
   int n = 0;
   for (int b = 0; b < p->batch_size; ++b) {

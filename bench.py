@@ -308,7 +308,8 @@ def cpu_prefill_sample(n_sample=8192, k_ret=K_RET, threads=None):
         w = OWT.wavelengths_sorted(D, THETA, k_ret)
         qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
         fn = lambda: OA.ref_window_attn(qn, kn, vn, w, phase="prefill", block_m=128, block_n=128)
-        kind, what = "port", "numpy restatement oracle/attention.py (the compiled reference was not built)"
+        kind, what = "port", ("numpy restatement oracle/attention.py (the reference's Python package is not "
+                              "on this machine)")
     t0 = time.perf_counter()
     fn()
     ms = (time.perf_counter() - t0) * 1e3
