@@ -22,7 +22,10 @@ ATF_NOALLOC_MAX_PARTIAL_ROWS = 16384
 EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_window_deff",
             "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
             "atf_rope_pack", "atf_paged_kv_append", "atf_status_string", "atf_version",
-            "atf_read_error_flag", "atf_selftest_wait_timeout", "atf_params_size")
+            "atf_read_error_flag", "atf_selftest_wait_timeout", "atf_params_size",
+            "atf_exchange_region_bytes", "atf_state_push", "atf_state_merge", "atf_ipc_export", "atf_ipc_import",
+            "atf_ipc_release")
+ATF_IPC_HANDLE_BYTES = 64
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
 
@@ -96,6 +99,13 @@ class AtfAppendParams(ctypes.Structure):
                 ("k_stride_head", _i64), ("k_stride_level", _i64)]
 
 
+class AtfExchangeParams(ctypes.Structure):
+    _fields_ = [("o", _vp), ("lse", _vp), ("o_stride_b", _i64), ("o_stride_h", _i64), ("batch", _i32),
+                ("num_heads", _i32), ("world", _i32), ("rank", _i32), ("peer_base", _vp), ("base", _vp),
+                ("out", _vp), ("out_stride_b", _i64), ("out_stride_h", _i64), ("out_dtype", ctypes.c_int),
+                ("lse_out", _vp), ("error_flag", _vp)]
+
+
 class AtfError(RuntimeError):
     """A non-zero status from the C ABI."""
 
@@ -136,10 +146,17 @@ def load() -> ctypes.CDLL:
             lib.atf_read_error_flag.argtypes = [_vp, P(ctypes.c_int)]
             lib.atf_selftest_wait_timeout.argtypes = [_vp, _vp]
             lib.atf_params_size.argtypes = [ctypes.c_char_p]
+            lib.atf_exchange_region_bytes.argtypes = [_i32, _i32, _i32]
+            lib.atf_state_push.argtypes = [P(AtfExchangeParams), _vp]
+            lib.atf_state_merge.argtypes = [P(AtfExchangeParams), _vp]
+            lib.atf_ipc_export.argtypes = [_vp, _vp, P(_i64)]
+            lib.atf_ipc_import.argtypes = [_vp, _i64, P(_vp), P(_vp)]
+            lib.atf_ipc_release.argtypes = [_vp]
             for name in EXPORTED:
-                if name not in ("atf_status_string", "atf_params_size"):
+                if name not in ("atf_status_string", "atf_params_size", "atf_exchange_region_bytes"):
                     getattr(lib, name).restype = ctypes.c_int
             lib.atf_params_size.restype = _i64
+            lib.atf_exchange_region_bytes.restype = _i64
             _lib = lib
     return _lib
 

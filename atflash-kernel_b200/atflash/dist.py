@@ -200,12 +200,139 @@ def merge_partials(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
     return _gather_and_merge(pack, B, H, D, group, world, merge_fn, out_dtype)
 
 
+class StateExchange:
+    """Cross-rank merge of partial attention states without a collective library
+    (atf_state_push / atf_state_merge): every rank writes its (O, LSE) state into
+    every peer's exchange region with NVLink peer stores and merges once every
+    peer's push of the step has arrived. The result is bit-identical to
+    all-gathering the states and merging them with lse_merge.
+
+    The exchange region is one zeroed device buffer per rank, mapped into the
+    peers' processes through CUDA IPC at construction (a collective setup step:
+    every rank of `group` constructs its StateExchange together). The step
+    counter lives on the device, so a step can be replayed from a CUDA graph.
+    """
+
+    def __init__(self, batch: int, num_heads: int, group=None, device=None, *, _emulate=None):
+        import ctypes
+        from . import _ffi
+        self.B, self.H = int(batch), int(num_heads)
+        self.rank, self.world = _rank_world(group) if _emulate is None else _emulate
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = _ffi.load()
+        nbytes = int(lib.atf_exchange_region_bytes(self.B, self.H, self.world))
+        if nbytes <= 0:
+            raise ValueError("unsupported exchange shape")
+        self._region = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+        self.base = (self._region.data_ptr() + 255) // 256 * 256
+        self._opened = []
+        self.peer_base = None
+        if _emulate is not None:
+            return  # peers are set by emulated()
+        ptrs = [self.base]
+        if self.world > 1:
+            handle = (ctypes.c_char * _ffi.ATF_IPC_HANDLE_BYTES)()
+            off = ctypes.c_int64(0)
+            with torch.cuda.device(self.device):
+                _ffi.check("atf_ipc_export", lib.atf_ipc_export(self.base, handle, ctypes.byref(off)))
+            torch.cuda.synchronize(self.device)  # the zeroed region is in place before any peer maps it
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, (bytes(handle), int(off.value)), group=group)
+            ptrs = []
+            for q, (h, o) in enumerate(everyone):
+                if q == self.rank:
+                    ptrs.append(self.base)
+                    continue
+                ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    _ffi.check("atf_ipc_import", lib.atf_ipc_import(h, o, ctypes.byref(ptr), ctypes.byref(base)))
+                self._opened.append(base.value)
+                ptrs.append(ptr.value)
+            self.group = group
+        self._set_peers(ptrs)
+
+    def _set_peers(self, ptrs):
+        self.peer_base = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+
+    @staticmethod
+    def emulated(batch: int, num_heads: int, world: int, device=None) -> List["StateExchange"]:
+        """`world` exchanges in one process on one GPU, wired with plain
+        pointers (no IPC): the ranks' pushes, then their merges, in that order,
+        reproduce a multi-GPU step on one device (tests)."""
+        xs = [StateExchange(batch, num_heads, device=device, _emulate=(r, world)) for r in range(world)]
+        for x in xs:
+            x._set_peers([y.base for y in xs])
+        return xs
+
+    def _params(self, o, lse):
+        from . import _ffi
+        if o.dtype != torch.float32 or tuple(o.shape) != (self.B, self.H, 128) or o.stride(2) != 1:
+            raise ValueError("the state must be fp32 (B, H, 128) with a contiguous head dim")
+        if lse.dtype != torch.float32 or tuple(lse.shape) != (self.B, self.H) or not lse.is_contiguous():
+            raise ValueError("the LSE must be a contiguous fp32 (B, H) tensor")
+        from . import _runtime
+        p = _ffi.AtfExchangeParams()
+        p.o, p.lse = o.data_ptr(), lse.data_ptr()
+        p.o_stride_b, p.o_stride_h = o.stride(0), o.stride(1)
+        p.batch, p.num_heads, p.world, p.rank = self.B, self.H, self.world, self.rank
+        p.peer_base, p.base = self.peer_base.data_ptr(), self.base
+        p.error_flag = _runtime.error_flag(self.device).data_ptr()
+        return p
+
+    def push(self, o: torch.Tensor, lse: torch.Tensor) -> None:
+        """Send this rank's state (O fp32 (B, H, 128), LSE natural log (B, H))."""
+        import ctypes
+        from . import _ffi, _runtime
+        p = self._params(o, lse)
+        with torch.cuda.device(self.device):
+            _ffi.check("atf_state_push", _ffi.load().atf_state_push(ctypes.byref(p), _runtime.stream_handle(self.device)))
+
+    def merge(self, o: torch.Tensor, lse: torch.Tensor, out=None, lse_out=None, out_dtype=torch.bfloat16):
+        """Merge every rank's state of this step into `out` (B, H, 128) and the
+        natural-log `lse_out` (B, H); o / lse are this rank's pushed state."""
+        import ctypes
+        from . import _ffi, _runtime
+        p = self._params(o, lse)
+        if out is None:
+            out = torch.empty((self.B, self.H, 128), dtype=out_dtype, device=self.device)
+        if lse_out is None:
+            lse_out = torch.empty((self.B, self.H), dtype=torch.float32, device=self.device)
+        p.out, p.out_stride_b, p.out_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+        p.out_dtype = _ffi.ATF_DTYPE_F32 if out.dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
+        p.lse_out = lse_out.data_ptr()
+        with torch.cuda.device(self.device):
+            _ffi.check("atf_state_merge",
+                       _ffi.load().atf_state_merge(ctypes.byref(p), _runtime.stream_handle(self.device)))
+        return out, lse_out
+
+    def close(self) -> None:
+        """Unmap the peers' regions (after every rank has finished its last step)."""
+        from . import _ffi
+        lib = _ffi.load()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for b in self._opened:
+                lib.atf_ipc_release(b)
+        self._opened = []
+
+
 def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
-                   kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16):
+                   kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16,
+                   exchange: Optional[StateExchange] = None):
     """Decode with this rank's KV shard; `wrapper` is planned over the rank's local
     pages. q_pos: global query position per request; kv_pos0: global position of
-    this rank's first key per request. Returns (out, lse) merged over the group."""
+    this rank's first key per request. Returns (out, lse) merged over the group:
+    through `exchange` (peer stores, no collective) when given, else with one
+    all-gather of the ranks' states."""
     _, world = _rank_world(group)
+    if exchange is not None:
+        B, H, D = q.shape
+        o = torch.empty((B, H, D), dtype=torch.float32, device=q.device)
+        lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
+        wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=o, lse=lse, return_lse=True,
+                    out_dtype=torch.float32)
+        exchange.push(o, lse)
+        return exchange.merge(o, lse, out_dtype=out_dtype)
     if world == 1:
         # one shard: the decode's own split merge is already the result
         return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
@@ -228,11 +355,13 @@ class ShardedDecodeStep:
     construction); `q_pos` / `kv_pos0` must be device tensors and may also be
     updated in place. Calling the object runs one step and returns (out, lse),
     tensors that later steps overwrite. The result equals ``sharded_decode`` on
-    the same inputs bit for bit.
+    the same inputs bit for bit. With a StateExchange the whole step (decode,
+    push, merge) is one graph and no collective runs at all.
     """
 
     def __init__(self, q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
-                 kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16):
+                 kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16,
+                 exchange: Optional["StateExchange"] = None):
         if not (q_pos.is_cuda and kv_pos0.is_cuda):
             raise ValueError("q_pos and kv_pos0 must be CUDA tensors (they are read by the replayed graph)")
         _, self.world = _rank_world(group)
@@ -241,12 +370,20 @@ class ShardedDecodeStep:
         self.q_pos, self.kv_pos0 = q_pos, kv_pos0
         B, H, D = q.shape
         self.B, self.H, self.D = B, H, D
+        self.exchange = exchange
         self.pack, self.o_view, self.l_view = _pack_views(B, H, D, q.device)
         n = self.pack.numel()
         self.allp = self.pack.new_empty((self.world * n,))
         from .decode import lse_merge
 
         def local():
+            if exchange is not None:
+                # the whole step (decode, push to the peers, merge) in one graph:
+                # no collective library call, the step counter is on the device
+                wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=self.o_view, lse=self.l_view,
+                            return_lse=True, out_dtype=torch.float32)
+                exchange.push(self.o_view, self.l_view)
+                return exchange.merge(self.o_view, self.l_view, out_dtype=out_dtype)
             if self.world == 1:
                 return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
                                    out_dtype=out_dtype)
@@ -261,7 +398,7 @@ class ShardedDecodeStep:
 
         # one eager step first (library load, lazy allocations), then the captures
         local()
-        if self.world > 1:
+        if self.world > 1 and exchange is None:
             dist.all_gather_into_tensor(self.allp, self.pack, group=group)
             merge()
         torch.cuda.synchronize()
@@ -272,7 +409,7 @@ class ShardedDecodeStep:
         with torch.cuda.stream(side):
             with torch.cuda.graph(self.g_local):
                 res = local()
-            if self.world > 1:
+            if self.world > 1 and exchange is None:
                 self.g_merge = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(self.g_merge):
                     res = merge()
@@ -281,7 +418,7 @@ class ShardedDecodeStep:
 
     def __call__(self):
         self.g_local.replay()
-        if self.world > 1:
+        if self.world > 1 and self.exchange is None:
             dist.all_gather_into_tensor(self.allp, self.pack, group=self.group)
             self.g_merge.replay()
         return self.out, self.lse

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "atflash", "_lib")
 LIB = os.path.join(OUT_DIR, "libatflash_b200.so")
-SOURCES = ["api.cu", "prefill_sm100.cu", "decode.cu", "decode_noalloc.cu", "rope.cu", "append.cu", "selftest.cu"]
+SOURCES = ["api.cu", "prefill_sm100.cu", "decode.cu", "decode_noalloc.cu", "exchange.cu", "rope.cu", "append.cu", "selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

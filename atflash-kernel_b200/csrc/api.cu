@@ -80,6 +80,7 @@ extern "C" int64_t atf_params_size(const char* name) {
       {"AtfMergeParams", static_cast<int64_t>(sizeof(AtfMergeParams))},
       {"AtfRopeParams", static_cast<int64_t>(sizeof(AtfRopeParams))},
       {"AtfAppendParams", static_cast<int64_t>(sizeof(AtfAppendParams))},
+      {"AtfExchangeParams", static_cast<int64_t>(sizeof(AtfExchangeParams))},
   };
   for (const Entry& e : kSizes)
     if (std::strcmp(e.n, name) == 0) return e.size;

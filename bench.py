@@ -604,11 +604,28 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
         step.release()
         res[name]["us_graph"] = ms_g * 1e3
         res[name]["gbs_aggregate_graph"] = total / (ms_g * 1e-3) / 1e9
+        if world > 1:
+            # the same step with the ranks' states exchanged by NVLink peer stores
+            # (atflash.dist.StateExchange) instead of the NCCL all-gather: eager,
+            # and the whole step replayed from one CUDA graph
+            ex = atflash.dist.StateExchange(B, hq)
+            ms_x, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0,
+                                                                  exchange=ex), steps, warmup, world)
+            xstep = atflash.dist.ShardedDecodeStep(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
+            ms_xg, _ = timed(lambda i: xstep(), steps, warmup, world)
+            xstep.release()
+            barrier(world)
+            ex.close()
+            barrier(world)
+            res[name]["us_exchange"] = ms_x * 1e3
+            res[name]["us_exchange_graph"] = ms_xg * 1e3
+            res[name]["gbs_aggregate_exchange_graph"] = total / (ms_xg * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
     res["parity"] = decode_1m_parity(device, rank, world, q, (kc, vc), perm, q_pos, kv_pos0, N, shard, page)
     res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, KV split into {world} shards, "
                      "all-gather of (O, LSE) + LSE merge inside the step; us: eager "
-                     "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep")
+                     "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep; us_exchange(_graph): "
+                     "the states exchanged by NVLink peer stores (atflash.dist.StateExchange), no collective")
     del kc, vc
     torch.cuda.empty_cache()
     return res

@@ -240,6 +240,52 @@ typedef struct {
 /* Merge partial attention states: LSE = log sum exp(LSE_i), O = sum exp(LSE_i - LSE) O_i. */
 int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream);
 
+/* ------------------------------------------------------------------ cross-rank state exchange */
+
+/* No counterpart in the reference, which runs on one GPU. The KV-sharded decode
+ * (the KV sequence split over the GPUs of one node) ends with every rank
+ * holding a partial state (O fp32 [B, H, 128], LSE natural log [B, H]); these
+ * calls merge the states of all ranks without a collective library: each rank
+ * pushes its state into every peer's exchange region with NVLink peer stores
+ * (no multicast), then merges once every peer's push of the step has arrived.
+ * The merge is the same arithmetic as atf_lse_merge on uniform parts, so the
+ * result is bit-identical to all-gathering the states and merging them.
+ *
+ * Exchange region: atf_exchange_region_bytes(B, H, world) bytes of device
+ * memory per rank, 256-byte aligned, zeroed once before the first step, and
+ * mapped into every other rank's process (atf_ipc_export / atf_ipc_import).
+ * Every rank calls atf_state_push and then atf_state_merge once per step, in
+ * the same order on one stream; the step counter lives in the region. A peer
+ * that does not push within the wait limit (2 s) leaves ATF_ERR_TIMEOUT's code
+ * in *error_flag and the merge returns without waiting further. */
+#define ATF_IPC_HANDLE_BYTES 64
+typedef struct {
+  const float* o;       /* this rank's state: fp32 [B, H, 128] (16-byte aligned) */
+  const float* lse;     /* fp32 [B, H], natural log, contiguous */
+  int64_t o_stride_b, o_stride_h;
+  int32_t batch, num_heads, world, rank;
+  void* const* peer_base; /* device array [world]: every rank's region as mapped here (own at [rank]) */
+  void* base;             /* this rank's region */
+  void* out;              /* [B, H, 128], bf16 or fp32 */
+  int64_t out_stride_b, out_stride_h;
+  int out_dtype;
+  float* lse_out;         /* optional [B, H], natural log */
+  int* error_flag;        /* optional device int */
+} AtfExchangeParams;
+
+int64_t atf_exchange_region_bytes(int32_t batch, int32_t num_heads, int32_t world);
+/* Push this rank's state into slot [step parity][rank] of every rank's region and
+ * signal each of them. */
+int atf_state_push(const AtfExchangeParams* p, atf_stream_t stream);
+/* Wait (bounded) for every rank's push of this step, merge, advance the step. */
+int atf_state_merge(const AtfExchangeParams* p, atf_stream_t stream);
+/* CUDA IPC of a device allocation: the handle of the allocation holding dev_ptr
+ * and dev_ptr's offset in it; import maps a peer's handle (ptr = base + offset);
+ * release unmaps a base returned by import. Setup calls, not for the step loop. */
+int atf_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int atf_ipc_import(const void* handle, int64_t offset, void** ptr_out, void** base_out);
+int atf_ipc_release(void* base);
+
 /* ------------------------------------------------------------------ RoPE */
 
 typedef struct {
@@ -302,7 +348,7 @@ const char* atf_status_string(int status);
 int atf_version(void);
 /* sizeof of the named params struct ("AtfPrefillParams", "AtfDecodePlanParams",
  * "AtfDecodePlan", "AtfDecodeParams", "AtfMergeParams", "AtfRopeParams",
- * "AtfAppendParams"), or -1: lets an FFI binding check its struct mirrors. */
+ * "AtfAppendParams", "AtfExchangeParams"), or -1: lets an FFI binding check its struct mirrors. */
 int64_t atf_params_size(const char* name);
 /* Synchronises the current device, copies *error_flag to *out and clears it. */
 int atf_read_error_flag(int* error_flag_device, int* out);

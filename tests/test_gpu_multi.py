@@ -5,7 +5,9 @@ K/V; the gathered rows must equal a one-GPU run bit for bit. KV-sharded decode:
 each rank decodes its contiguous shard of every request with global positions,
 the partial (O, LSE) are all-gathered and merged; the result must match the
 one-GPU decode of the whole cache (same kernels, different split points, so a
-tolerance rather than bit equality)."""
+tolerance rather than bit equality). The NVLink state exchange (peer stores, no
+collective) must equal the all-gather path bit for bit, eagerly and replayed
+from a CUDA graph."""
 import os
 import socket
 
@@ -108,7 +110,25 @@ def _worker(rank, world, port, errq):
         torch.cuda.synchronize()
         assert torch.equal(o_g, out2) and torch.equal(l_g, lse2), "graph step on a new query differs"
         step.release()
+        # the same step through the NVLink state exchange (peer stores, no
+        # collective): bit-identical to the all-gather path, over several steps
+        # and from a CUDA graph
+        ex = atflash.dist.StateExchange(len(lens), hq)
+        for _ in range(3):
+            ox, lx = atflash.dist.sharded_decode(step.q, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                                 out_dtype=torch.float32, exchange=ex)
+            torch.cuda.synchronize()
+            assert torch.equal(ox, out2) and torch.equal(lx, lse2), "exchange differs from the all-gather path"
+        gstep = atflash.dist.ShardedDecodeStep(step.q, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                               out_dtype=torch.float32, exchange=ex)
+        for _ in range(3):
+            og, lg = gstep()
+        torch.cuda.synchronize()
+        assert torch.equal(og, out2) and torch.equal(lg, lse2), "graph-replayed exchange step differs"
+        gstep.release()
         assert atflash.check_device_errors() == 0
+        dist.barrier()
+        ex.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report to the parent, which fails the test

@@ -98,6 +98,19 @@ def test_invalid_arguments_rejected_without_gpu():
     r.x, r.out, r.cos, r.sin = 16, 16, 32, 48
     r.head_dim, r.n_pos, r.cs_stride_pos = 128, 1, 64
     assert lib.atf_rope_pack(ctypes.byref(r), None) == -1  # in place
+    assert lib.atf_state_push(None, None) == -1
+    assert lib.atf_state_merge(None, None) == -1
+    x = _ffi.AtfExchangeParams()
+    x.o = x.lse = x.peer_base = x.base = 256
+    x.batch, x.num_heads, x.world, x.rank = 1, 28, 2, 2  # rank outside the group
+    assert lib.atf_state_push(ctypes.byref(x), None) == -1
+    x.rank = 1
+    x.base = 272  # the region must be 256-byte aligned
+    assert lib.atf_state_push(ctypes.byref(x), None) == -3
+    # region: 2 parities x world x (B*H*128 + round4(B*H)) floats, flags, step, tickets
+    S = 28 * 128 + 28
+    assert lib.atf_exchange_region_bytes(1, 28, 8) == ((2 * 8 * S * 4 + 8 * 8 + 8 + 8) + 255) // 256 * 256
+    assert lib.atf_exchange_region_bytes(0, 28, 8) == -1
 
 
 def test_decode_run_rejects_misaligned_workspace_and_output():
