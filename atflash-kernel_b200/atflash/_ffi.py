@@ -40,7 +40,8 @@ class AtfPrefillParams(ctypes.Structure):
                 ("o_stride_b", _i64), ("o_stride_s", _i64), ("o_stride_h", _i64),
                 ("q_offset", _i64), ("softmax_scale", _f32), ("causal", ctypes.c_int),
                 ("qk_layout", ctypes.c_int), ("window", ctypes.c_int), ("zhi", _i32 * 8),
-                ("error_flag", _vp)]
+                ("error_flag", _vp), ("q_cos", _vp), ("q_sin", _vp), ("q_cs_stride_pos", _i64),
+                ("q_n_pos", _i64)]
 
 
 class AtfDecodePlanParams(ctypes.Structure):

@@ -56,8 +56,13 @@ def _check_qkv(q, k, v):
 def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
                 softmax_scale: Optional[float] = None, window_table: WindowSpec = None,
                 qk_layout: str = "sorted_pair", q_offset: Optional[int] = None,
-                out: Optional[torch.Tensor] = None, return_lse: bool = False):
-    """Run the tcgen05 windowed prefill kernel. q (B, Sq, Hq, 128), k/v (B, Sk, Hkv, 128)."""
+                out: Optional[torch.Tensor] = None, return_lse: bool = False,
+                q_rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+    """Run the tcgen05 windowed prefill kernel. q (B, Sq, Hq, 128), k/v (B, Sk, Hkv, 128).
+
+    q_rope: optional fp32 (cos, sin) tables (n_pos, >= 64): q is then pre-RoPE in
+    rotate_half order and the kernel rotates each query row at position
+    q_offset + row as it loads it (k must be post-RoPE, sorted pairs)."""
     _check_qkv(q, k, v)
     dev = _runtime.require_cuda(q, k, v)
     B, Sq, Hq, D = q.shape
@@ -93,6 +98,18 @@ def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bo
         for i, z in enumerate(zhi):
             p.zhi[i] = z
     p.error_flag = _runtime.error_flag(dev).data_ptr()
+    if q_rope is not None:
+        cos, sin = q_rope
+        if qk_layout != "sorted_pair":
+            raise ValueError("RoPE at load needs k in sorted-pair order")
+        if (cos.dtype != torch.float32 or sin.dtype != torch.float32 or cos.shape != sin.shape or cos.dim() != 2
+                or cos.shape[1] < 64 or cos.stride(1) != 1 or cos.stride() != sin.stride() or not cos.is_cuda
+                or cos.device != dev or sin.device != dev):
+            raise ValueError("q_rope must be matching fp32 (n_pos, >=64) tables on the tensors' device")
+        if cos.shape[0] < q_offset + Sq:
+            raise ValueError(f"the RoPE tables cover {cos.shape[0]} positions, the queries need {q_offset + Sq}")
+        p.q_cos, p.q_sin = cos.data_ptr(), sin.data_ptr()
+        p.q_cs_stride_pos, p.q_n_pos = cos.stride(0), cos.shape[0]
     with torch.cuda.device(dev):
         rc = _ffi.load().atf_prefill_fwd(ctypes.byref(p), _runtime.stream_handle(dev))
     _ffi.check("atf_prefill_fwd", rc)
@@ -111,9 +128,9 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
     qk_layout: pair order of q/k along head_dim: "sorted_pair" (the reference's
       kernel layout) or "rotate_half" (HF order; read in place, no permute copy).
     rope: optional (cos, sin) fp32 tables of shape (n_pos, 64); when given, q and k
-      are pre-RoPE in rotate_half order and are rotated first (query i at position
-      q_offset + i, key n at position n), into the sorted-pair order the kernel
-      reads fastest.
+      are pre-RoPE in rotate_half order (query i at position q_offset + i, key n at
+      position n). k is rotated into sorted-pair order first (one pass); q is
+      rotated by the prefill kernel itself as it loads each query tile.
     Returns out, or (out, softmax_lse, None) when return_attn_probs.
     """
     if dropout_p != 0.0:
@@ -122,15 +139,15 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
         raise NotImplementedError("sliding-window (window_size) is not supported; use window_table")
     if softcap != 0.0 or alibi_slopes is not None:
         raise NotImplementedError("softcap / alibi are not supported")
+    q_rope = None
     if rope is not None:
         cos, sin = rope
-        Sq, Sk = q.shape[1], k.shape[1]
-        off = (Sk - Sq) if q_offset is None else q_offset
-        q = rope_pack(q, cos, sin, pos_offset=off, out_layout="sorted_pair")
         k = rope_pack(k, cos, sin, pos_offset=0, out_layout="sorted_pair")
         qk_layout = "sorted_pair"
+        q_rope = (cos, sin)
     res = prefill_fwd(q, k, v, causal=causal, softmax_scale=softmax_scale, window_table=window_table,
-                      qk_layout=qk_layout, q_offset=q_offset, out=out, return_lse=return_attn_probs)
+                      qk_layout=qk_layout, q_offset=q_offset, out=out, return_lse=return_attn_probs,
+                      q_rope=q_rope)
     if return_attn_probs:
         return res[0], res[1], None
     return res

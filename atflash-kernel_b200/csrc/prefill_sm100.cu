@@ -47,6 +47,7 @@
 
 #include "atf_internal.h"
 #include "atf_ptx.cuh"
+#include "rope_math.cuh"
 
 namespace atf {
 namespace prefill {
@@ -169,6 +170,13 @@ struct Args {
   long long o_sb, o_ss, o_sh;
   float* lse;
   int* err;
+  // RoPE of q at load (qrot): the pre-RoPE rows and the fp32 cos / sin tables
+  int qrot;
+  const __nv_bfloat16* q;
+  long long q_sb, q_ss, q_sh;
+  const float* qcos;
+  const float* qsin;
+  long long cs_stride;
 };
 
 __device__ __forceinline__ int levels_for(const Args& a, int row0, int j) {
@@ -246,7 +254,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     *s_abort = (a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0) ? 1 : 0;
-    mbar_init(bar(B_Q), 1);
+    // Q arrives by TMA (one expect_tx arrival), or rotated by the softmax threads
+    mbar_init(bar(B_Q), a.qrot ? NQ * 128 : 1);
     for (int s = 0; s < KST; ++s) {
       mbar_init(bar(B_KFULL + s), 1);
       mbar_init(bar(B_KEMPTY + s), 1);
@@ -287,7 +296,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // issues each TMA / expect_tx.
     int issued_k = 0, issued_v = 0;
     bool ok = true;
-    {
+    if (!a.qrot) {
       uint32_t qbytes = 0;
 #pragma unroll
       for (int t = 0; t < NQ; ++t) qbytes += nk[t] > 0 ? QTILE_BYTES : 0u;
@@ -437,6 +446,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int qrow = my_row0 + r;
     const long long qpos = a.q_offset + qrow;
     const float sl2 = a.scale_log2;
+    if (a.qrot) {
+      // RoPE at load: this thread's query row, rotated in fp32 at its position,
+      // rounded to bf16, into the sorted-pair Q slabs (level i = HF pairs
+      // 8(7-i)..8(7-i)+7); rows past the end are zero
+      uint8_t* qt = sp + OFF_Q + t * QTILE_BYTES + r * 16;
+      const bool valid = my_nk > 0 && qrow < a.Sq;
+      const __nv_bfloat16* xr = a.q + static_cast<long long>(bi) * a.q_sb + static_cast<long long>(qrow) * a.q_ss +
+                                static_cast<long long>(h) * a.q_sh;
+      const float* cr = a.qcos + qpos * a.cs_stride;
+      const float* sr = a.qsin + qpos * a.cs_stride;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (valid) ropemath::rotate_chunk_sorted_words(xr, cr, sr, c, w);
+        uint8_t* slab = qt + (7 - c) * QSLAB_BYTES;
+        *reinterpret_cast<uint4*>(slab) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(slab + QHALF_BYTES) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      // the MMAs read Q through the async proxy
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(bar(B_Q));
+    }
     float m2 = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < my_nk; ++j) {
@@ -589,6 +620,15 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
                                p->v_stride_h, p->o_stride_b, p->o_stride_s, p->o_stride_h};
   for (int i = 0; i < 12; ++i)
     if (strides[i] < 0 || (strides[i] & 7) != 0) return ATF_ERR_ALIGNMENT;
+  const bool qrot = p->q_cos != nullptr || p->q_sin != nullptr;
+  if (qrot) {
+    // q is pre-RoPE rotate_half; k must already be post-RoPE sorted pairs
+    if (p->q_cos == nullptr || p->q_sin == nullptr || p->qk_layout != ATF_LAYOUT_SORTED_PAIR ||
+        p->q_cs_stride_pos < 64 || p->q_n_pos < p->q_offset + p->seqlen_q)
+      return ATF_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(p->q_cos) & 3) || (reinterpret_cast<uintptr_t>(p->q_sin) & 3))
+      return ATF_ERR_ALIGNMENT;
+  }
   if (p->window == ATF_WINDOW_SNAP16) {
     for (int i = 0; i < ATF_MAX_LEVELS; ++i)
       if (p->zhi[i] < 0 || (i > 0 && p->zhi[i] > p->zhi[i - 1])) return ATF_ERR_INVALID_ARG;
@@ -659,6 +699,14 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
   a.o_sh = p->o_stride_h;
   a.lse = p->lse;
   a.err = p->error_flag;
+  a.qrot = qrot ? 1 : 0;
+  a.q = static_cast<const __nv_bfloat16*>(p->q);
+  a.q_sb = p->q_stride_b;
+  a.q_ss = p->q_stride_s;
+  a.q_sh = p->q_stride_h;
+  a.qcos = p->q_cos;
+  a.qsin = p->q_sin;
+  a.cs_stride = p->q_cs_stride_pos;
 
   if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(SMEM_BYTES)) != cudaSuccess)

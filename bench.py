@@ -700,6 +700,77 @@ def decode_1m_parity(device, rank, world, q, cache, perm, q_pos, kv_pos0, N, sha
     return out
 
 
+def bench_request(device, n_ctx=32768, chunk=8192, new_tokens=64, k_ret=2.0, reps=2):
+    """Whole-request timing with the window on and off, as the reference's
+    harness times a request (e2e_pipeline/atflash_e2e_fafi.py:200-265,
+    run_pass): a Qwen2.5-7B-1M-shaped model (28 layers, 3584 hidden, 28 / 4
+    heads, head_dim 128, rope_theta 1e7) with random bf16 weights (no checkpoint
+    is available here; speed does not depend on the weights) runs every
+    attention through atflash.hf. One request: chunked prefill of n_ctx random
+    tokens (chunk rows per forward, the KV cache growing), then new_tokens greedy
+    decode steps. Prefill and decode are timed with CUDA events; the best of
+    `reps` passes per mode is reported."""
+    from transformers import DynamicCache, Qwen2Config, Qwen2ForCausalLM
+    import atflash.hf
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+                      num_attention_heads=28, num_key_value_heads=4, max_position_embeddings=1010000,
+                      rope_theta=1e7, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16).eval()
+    name = atflash.hf.register(model, k_ret_prefill=k_ret, k_ret_decode=k_ret)
+    model.set_attn_implementation(name)
+    tables = atflash.hf.window_tables_for_model(model, k_ret, k_ret)
+    ids = torch.randint(0, cfg.vocab_size, (1, n_ctx), generator=torch.Generator().manual_seed(5)).to(device)
+
+    @torch.inference_mode()
+    def run_pass():
+        ev = lambda: torch.cuda.Event(enable_timing=True)
+        cache = DynamicCache()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for cs in range(0, n_ctx, chunk):
+            out = model(input_ids=ids[:, cs:cs + chunk], use_cache=True, past_key_values=cache, logits_to_keep=1)
+            cache = out.past_key_values
+        e1.record()
+        cur = out.logits[:, -1, :].argmax(-1, keepdim=True)
+        steps = []
+        for _ in range(new_tokens):
+            s0, s1 = ev(), ev()
+            s0.record()
+            out = model(input_ids=cur, use_cache=True, past_key_values=cache)
+            s1.record()
+            cache = out.past_key_values
+            cur = out.logits[:, -1, :].argmax(-1, keepdim=True)
+            steps.append((s0, s1))
+        torch.cuda.synchronize()
+        step_ms = sorted(a.elapsed_time(b) for a, b in steps)
+        return {"prefill_ms": e0.elapsed_time(e1), "decode_step_ms_median": step_ms[len(step_ms) // 2],
+                "decode_ms_total": sum(step_ms)}
+
+    res = {}
+    for mode in ("on", "off"):
+        atflash.hf.configure(*(tables if mode == "on" else (None, None)))
+        best = None
+        for _ in range(reps + 1):  # the first pass warms up
+            r = run_pass()
+            if best is None or r["prefill_ms"] + r["decode_ms_total"] < best["prefill_ms"] + best["decode_ms_total"]:
+                best = r
+        best["total_ms"] = best["prefill_ms"] + best["decode_ms_total"]
+        res[mode] = best
+    atflash.hf.configure(None, None)
+    res["ratio_on_off_prefill"] = res["off"]["prefill_ms"] / res["on"]["prefill_ms"]
+    res["ratio_on_off_decode"] = res["off"]["decode_ms_total"] / res["on"]["decode_ms_total"]
+    res["ratio_on_off_total"] = res["off"]["total_ms"] / res["on"]["total_ms"]
+    res["device_error_flag"] = atflash.check_device_errors()
+    res["config"] = (f"Qwen2.5-7B-1M shape, random bf16 weights, 1 request: {n_ctx}-token prefill in {chunk}-token "
+                     f"chunks + {new_tokens} greedy decode steps, window k={k_ret:g} (theta 1e7) vs off, "
+                     f"all attention through atflash.hf; best of {reps} passes")
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
     """512K-token windowed prefill (k=2), 28/4 heads, zig-zag
     query blocks over the ranks with K/V replicated; max-over-ranks ms."""
@@ -737,9 +808,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="atflash", choices=["atflash", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip off/k64/decode/e2e/cpu legs")
-    ap.add_argument("--only", default="all", choices=["all", "prefill", "decode", "decode1m", "prefill512k"],
+    ap.add_argument("--only", default="all",
+                    choices=["all", "prefill", "decode", "decode1m", "prefill512k", "request"],
                     help="prefill: the headline leg alone; decode: the config-3 decode leg alone; "
-                         "decode1m / prefill512k: the config-5 / config-4 legs alone")
+                         "decode1m / prefill512k: the config-5 / config-4 legs alone; request: whole-request "
+                         "on/off timing on a random-weight Qwen2.5-7B-1M-shaped model (1 GPU)")
     ap.add_argument("--seq-len", type=int, default=131072,
                     help="sequence length (smaller values are for profiling captures)")
     args = ap.parse_args()
@@ -759,6 +832,11 @@ def main():
         res = bench_decode(device, args.steps, args.warmup, peaks, N=args.seq_len)
         if rank == 0:
             print(json.dumps({"decode": res}), flush=True)
+        return
+    if args.only == "request":
+        res = bench_request(device, n_ctx=min(args.seq_len, 131072))
+        if rank == 0:
+            print(json.dumps({"request": res}), flush=True)
         return
     if args.only in ("decode1m", "prefill512k"):
         fn = bench_decode_1m if args.only == "decode1m" else bench_prefill_512k
@@ -836,9 +914,20 @@ def main():
         sets = [tuple(torch.empty(t.shape, dtype=t.dtype, device=device) for t in (qh, kh, vh, qh))
                 for _ in range(2)]
         chunks = e2e_chunks(blocks)
-        h2d = (kh.numel() + vh.numel()) * 2 + sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
+        # K/V: with one GPU the copy stream sends each chunk's new key rows; with
+        # several, every rank sends only its 1/N share of each of KV_CHUNKS key
+        # ranges and an all-gather over NVLink (in place, on a third stream)
+        # completes the range on every rank before the query chunks that need it
+        KV_CHUNKS = 16
+        kv_bounds = [N_CTX * c // KV_CHUNKS for c in range(KV_CHUNKS + 1)]
+        shard_kv = world > 1 and all((kv_bounds[c + 1] - kv_bounds[c]) % world == 0 for c in range(KV_CHUNKS))
+        kv_h2d = (kh.numel() + vh.numel()) * 2 // (world if shard_kv else 1)
+        h2d = kv_h2d + sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         d2h = sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        comm = torch.cuda.Stream(device) if shard_kv else None
+        ev_up = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
+        ev_kv = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
         ev_q = [torch.cuda.Event() for _ in chunks]
         ev_o = [torch.cuda.Event() for _ in chunks]
         ev_in_free = [torch.cuda.Event() for _ in range(2)]   # the set's inputs are no longer read
@@ -854,19 +943,43 @@ def main():
                 up.wait_event(ev_in_free[b])
             else:
                 up.wait_stream(main)
-            with torch.cuda.stream(up):
-                kv_sent = 0
-                for n, (c0, c1) in enumerate(chunks):
-                    if c1 > kv_sent:
-                        kd[:, kv_sent:c1].copy_(kh[:, kv_sent:c1], non_blocking=True)
-                        vd[:, kv_sent:c1].copy_(vh[:, kv_sent:c1], non_blocking=True)
-                        kv_sent = c1
-                    qd[:, c0:c1].copy_(qh[:, c0:c1], non_blocking=True)
-                    ev_q[n].record(up)
+            if shard_kv:
+                with torch.cuda.stream(up):
+                    for c in range(KV_CHUNKS):
+                        a0, a1 = kv_bounds[c], kv_bounds[c + 1]
+                        part = (a1 - a0) // world
+                        p0 = a0 + rank * part
+                        kd[:, p0:p0 + part].copy_(kh[:, p0:p0 + part], non_blocking=True)
+                        vd[:, p0:p0 + part].copy_(vh[:, p0:p0 + part], non_blocking=True)
+                        ev_up[c].record(up)
+                    for n, (c0, c1) in enumerate(chunks):
+                        qd[:, c0:c1].copy_(qh[:, c0:c1], non_blocking=True)
+                        ev_q[n].record(up)
+                with torch.cuda.stream(comm):
+                    for c in range(KV_CHUNKS):
+                        a0, a1 = kv_bounds[c], kv_bounds[c + 1]
+                        part = (a1 - a0) // world
+                        p0 = a0 + rank * part
+                        comm.wait_event(ev_up[c])
+                        for t in (kd, vd):
+                            dist.all_gather_into_tensor(t[:, a0:a1].reshape(-1), t[:, p0:p0 + part].reshape(-1))
+                        ev_kv[c].record(comm)
+            else:
+                with torch.cuda.stream(up):
+                    kv_sent = 0
+                    for n, (c0, c1) in enumerate(chunks):
+                        if c1 > kv_sent:
+                            kd[:, kv_sent:c1].copy_(kh[:, kv_sent:c1], non_blocking=True)
+                            vd[:, kv_sent:c1].copy_(vh[:, kv_sent:c1], non_blocking=True)
+                            kv_sent = c1
+                        qd[:, c0:c1].copy_(qh[:, c0:c1], non_blocking=True)
+                        ev_q[n].record(up)
             if used[b]:
                 main.wait_event(ev_out_free[b])
             for n, (c0, c1) in enumerate(chunks):
                 main.wait_event(ev_q[n])
+                if shard_kv:  # every key range below c1 has been gathered
+                    main.wait_event(ev_kv[next(c for c in range(KV_CHUNKS) if kv_bounds[c + 1] >= c1)])
                 atflash.flash_attn_func(qd[:, c0:c1], kd[:, :c1], vd[:, :c1], causal=True, window_table=wt2,
                                         q_offset=c0, out=outd[:, c0:c1])
                 ev_o[n].record(main)
@@ -876,6 +989,10 @@ def main():
             ev_in_free[b].record(main)
             ev_out_free[b].record(down)
             used[b] = True
+            if shard_kv:
+                # the next step on this buffer set overwrites K/V only after this
+                # step's gathers are done
+                main.wait_stream(comm)
             if i == n_e2e - 1:
                 # the timed region ends after the last step's copies
                 main.wait_stream(down)
@@ -883,7 +1000,10 @@ def main():
         ms_e2e, _ = timed(e2e_fn, n_e2e, 3, world)
         e2e = {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "pipeline": f"{len(chunks)} query chunks per step (2048 growing to 16384 rows, last 4096) in "
-                           f"ascending order; a copy stream sends each chunk's new k/v rows and its q rows, "
+                           f"ascending order; " + (f"each rank sends 1/{world} of every one of {KV_CHUNKS} k/v row "
+                           f"ranges and an NCCL all-gather over NVLink completes each range on every rank; a copy "
+                           f"stream sends the rank's q rows, " if shard_kv else
+                           f"a copy stream sends each chunk's new k/v rows and its q rows, ") +
                            f"and each chunk's output goes down on another while later chunks compute; two "
                            f"device buffer sets alternate by step, so a step's copies overlap the previous "
                            f"step's compute; the last step's copies complete inside the timed region"}

@@ -111,11 +111,23 @@ typedef struct {
   int window;          /* ATF_WINDOW_OFF or ATF_WINDOW_SNAP16 */
   int32_t zhi[ATF_MAX_LEVELS]; /* 16-snap levels; zhi[0] must cover every distance */
   int* error_flag;     /* optional device int (see header comment) */
+  /* RoPE of q at load (optional): with q_cos / q_sin given, q is the PRE-RoPE
+   * query in HF rotate_half order; each query row is rotated at position
+   * q_offset + row in fp32 (x1*cos - x2*sin, x2*cos + x1*sin, separately rounded
+   * products), rounded to bf16 and placed in sorted-pair order as the kernel
+   * loads it. k must then be post-RoPE in sorted-pair order (qk_layout). The
+   * tables are fp32 [q_n_pos, >= 64]; row p holds cos / sin(p * inv_freq). */
+  const float* q_cos;
+  const float* q_sin;
+  int64_t q_cs_stride_pos; /* elements between the tables' rows */
+  int64_t q_n_pos;         /* rows in the tables; q_offset + seqlen_q <= q_n_pos */
 } AtfPrefillParams;
 
 /* Windowed causal prefill on the tcgen05/TMEM kernel. Tiles are 128 queries x
  * 128 keys; the window is quantised per (q-tile, k-tile) at the tile's smallest
- * distance, as atflash/reference.py:27-80 with block_m = block_n = 128. */
+ * distance, as atflash/reference.py:27-80 with block_m = block_n = 128. With
+ * q_cos / q_sin the RoPE of q is applied at load (the RoPE front-end of
+ * microbench/b1_correctness.py:113-135 for q, fused into the kernel). */
 int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream);
 
 /* ------------------------------------------------------------------ decode */

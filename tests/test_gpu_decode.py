@@ -312,6 +312,20 @@ def test_prefill_with_rope_end_to_end(cuda_device):
                              block_m=128, block_n=128)
     mx, mean = err_stats(out.transpose(1, 2).float().cpu().numpy(), ref)
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL
+    # q is rotated inside the prefill as it is loaded: bit-identical to running
+    # the kernel on the front-end's post-RoPE sorted-pair tensors
+    pre = atflash.flash_attn_func(q.transpose(1, 2).contiguous().to(dev), k.transpose(1, 2).contiguous().to(dev),
+                                  v.transpose(1, 2).contiguous().to(dev), causal=True,
+                                  window_table=atflash.WindowTable(128, 5e5, 2.0))
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), pre.view(torch.int16))
+    # a chunk of the queries (rows 384..639 at positions 384..639) against all keys
+    part = atflash.flash_attn_func(q0.transpose(1, 2)[:, 384:].contiguous().to(dev),
+                                   k0.transpose(1, 2).contiguous().to(dev), v.transpose(1, 2).contiguous().to(dev),
+                                   causal=True, window_table=atflash.WindowTable(128, 5e5, 2.0),
+                                   rope=(cos.to(dev), sin.to(dev)), q_offset=384)
+    torch.cuda.synchronize()
+    assert torch.equal(part.view(torch.int16), out[:, 384:].view(torch.int16))
 
 
 def _level_major(kc):
