@@ -59,9 +59,7 @@ class BatchDecodeWithPagedKVCacheWrapper:
             need = 4 * (P["po_floats"] + P["pl_floats"]) + 256
             if self._ws.numel() * self._ws.element_size() < need:
                 raise ValueError(f"workspace too small for the current plan: need {need} bytes")
-            ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
-            base = (ws.data_ptr() + 255) // 256 * 256
-            self._tmpl.partial_o, self._tmpl.partial_lse = base, base + 4 * P["po_floats"]
+            self._bind_workspace()
 
     def plan(self, indptr, indices, last_page_len, num_qo_heads: int, num_kv_heads: int,
              head_dim: int, page_size: int, pos_encoding_mode: str = "NONE", window_left: int = -1,
@@ -171,11 +169,17 @@ class BatchDecodeWithPagedKVCacheWrapper:
             t.zhi16[i] = zhi16[i]
         for i in range(16):
             t.zhi8[i] = zhi8[i]
+        t.error_flag = _runtime.error_flag(dev).data_ptr()
+        self._tmpl = t
+        self._bind_workspace()
+
+    def _bind_workspace(self):
+        """Point the launch template at the workspace: partial outputs, then
+        partial LSEs."""
+        P, t = self._plan, self._tmpl
         ws = self._ws.view(torch.uint8) if self._ws.dtype != torch.uint8 else self._ws
         base = (ws.data_ptr() + 255) // 256 * 256
         t.partial_o, t.partial_lse = base, base + 4 * P["po_floats"]
-        t.error_flag = _runtime.error_flag(dev).data_ptr()
-        self._tmpl = t
 
     begin_forward = plan
 

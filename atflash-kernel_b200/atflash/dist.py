@@ -145,20 +145,26 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=
 
 def gather_zigzag(outs, seqlen: int, world: int, group=None, zhi: Optional[Sequence[int]] = None) -> torch.Tensor:
     """All-gather every rank's two blocks into the full output (rows in order).
-    `zhi` must be the window levels the blocks were cut with (None: equal rows)."""
+    `zhi` must be the window levels the blocks were cut with (None: equal rows).
+
+    Every rank writes its blocks into its own slot of one padded receive buffer
+    and the all-gather runs in place, so the only copies besides the gather are
+    this rank's blocks going in and every block going to its rows in the output."""
     bounds = zigzag_bounds(seqlen, world, zhi=zhi)
     maxlen = max(bounds[i + 1] - bounds[i] for i in range(2 * world))
     ref = outs[0][2]
     B, _, H, D = ref.shape
-    send = ref.new_zeros((2, B, maxlen, H, D))
-    for t, (s, e, o) in enumerate(outs):
-        send[t, :, : e - s] = o
+    rank, _ = _rank_world(group)
     recv = ref.new_empty((world, 2, B, maxlen, H, D))
-    dist.all_gather_into_tensor(recv.view(-1), send.view(-1), group=group)
+    for t, (s, e, o) in enumerate(outs):
+        if e > s:
+            recv[rank, t, :, : e - s].copy_(o)
+    dist.all_gather_into_tensor(recv.view(-1), recv[rank].view(-1), group=group)
     full = ref.new_empty((B, seqlen, H, D))
     for r in range(world):
         for t, (s, e) in enumerate(zigzag_blocks(seqlen, world, r, zhi=zhi)):
-            full[:, s:e] = recv[r, t, :, : e - s]
+            if e > s:
+                full[:, s:e].copy_(recv[r, t, :, : e - s])
     return full
 
 

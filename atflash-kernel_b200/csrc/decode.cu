@@ -143,6 +143,9 @@ __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
 }
 
 __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
+  // the split merge that follows on the stream may be scheduled now; it waits
+  // for this grid's completion before reading the partial states
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -422,6 +425,9 @@ __global__ void __launch_bounds__(THREADS, 2)
     decode_tma_kernel(const __grid_constant__ KMaps tmK, const __grid_constant__ CUtensorMap tmV,
                       const Args args) {
   extern __shared__ uint8_t smem_raw[];
+  // the split merge that follows on the stream may be scheduled now; it waits
+  // for this grid's completion before reading the partial states
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const decode::Args& a = args.d;
   const uint32_t raw = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -477,7 +483,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     // the item's page list, staged once so that no TMA waits on a global load
     int* s_pages = reinterpret_cast<int*>(sp + OFF_PAGES);
     const int first_page = k_beg / a.page_size;
-    const int n_item_pages = (k_end - 1) / a.page_size - first_page + 1;
+    const int n_item_pages = k_end > k_beg ? (k_end - 1) / a.page_size - first_page + 1 : 0;
     for (int i = lane; i < n_item_pages; i += 32) s_pages[i] = a.indices[pg0 + first_page + i];
     __syncwarp();
     int issued = 0;
@@ -955,7 +961,9 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   m.o_sh = p->o_stride_h;
   m.out_f32 = p->out_dtype == ATF_DTYPE_F32 ? 1 : 0;
   m.lse_out = p->lse_out;
-  return merge::launch(m, st);
+  // launched as a programmatic dependent of the decode kernel: its launch
+  // overlaps the decode's last wave, and it waits for the decode to complete
+  return merge::launch(m, st, /*after_decode=*/p->num_items > 0);
 }
 
 extern "C" int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream) {

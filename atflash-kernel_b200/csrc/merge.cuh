@@ -65,6 +65,9 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Ar
   const int bh = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = bh / a.H, h = bh % a.H;
+  // launched as a programmatic dependent of the decode kernel: wait until that
+  // grid has completed and its partial states are visible (immediate otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float* po = a.po;
   const float* pl = a.pl;
   if (a.wait_flags != nullptr) {
@@ -197,11 +200,27 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Ar
   }
 }
 
-static int launch(const Args& a, cudaStream_t stream) {
+// after_decode: launch with programmatic stream serialization, so that the
+// launch overlaps the decode kernel just issued on the stream (the kernel's
+// griddepcontrol.wait still orders every read after that grid's completion).
+static int launch(const Args& a, cudaStream_t stream, bool after_decode = false) {
   const long long blocks = static_cast<long long>(a.B) * a.H;
   if (blocks > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
-  merge_kernel<<<static_cast<unsigned>(blocks), MERGE_WARPS * 32, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
+  if (!after_decode) {
+    merge_kernel<<<static_cast<unsigned>(blocks), MERGE_WARPS * 32, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(MERGE_WARPS * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_kernel, a) == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
 }
 
 }  // namespace merge

@@ -112,6 +112,23 @@ def test_decode_parity(cuda_device, case, window):
     assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
 
 
+def test_decode_with_an_empty_request(cuda_device):
+    """A batch holding an empty request (no keys, no split items): its output
+    is zeros and its LSE -inf; the other requests match the oracle."""
+    import atflash
+    kv_lens, hq, hkv, page = [700, 0, 300], 6, 2, 16
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, page, seed=77)
+    lpl[1] = 1
+    wt = atflash.WindowTable(128, 1e4, 2.0)
+    out, lse = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", wt,
+                          return_lse=True)
+    for b in (0, 2):
+        ref = oracle_decode(q[b:b + 1], ks[b:b + 1], vs[b:b + 1], 1e4, 2.0)
+        mx, mean = err_stats(out[b:b + 1].float().cpu().numpy(), ref)
+        assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (b, mx, mean)
+    assert torch.all(out[1] == 0) and torch.all(torch.isinf(lse[1]))
+
+
 def test_decode_many_splits_and_lse(cuda_device):
     """Force 64-key items so a request spans dozens of splits; the merged output
     and LSE match the oracle."""
