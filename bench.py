@@ -771,6 +771,86 @@ def bench_request(device, n_ctx=32768, chunk=8192, new_tokens=64, k_ret=2.0, rep
     return res
 
 
+def bench_reference_decode_kernel(device, peaks, N=131072, steps=50, warmup=10):
+    """The reference's own windowed decode kernel beside this repository's, on
+    the same single request on this GPU: FlashInfer's single-request decode
+    with the reference's window diff (kernels/flashinfer_port/*.diff), built by
+    oracle/build_fi_ref.py into oracle/_ref/fi_atfwin.so, called as the
+    reference's harness calls it (e2e_pipeline/atflash_e2e_fafi.py:106-110:
+    q [Hq, d], contiguous k / v [N, Hkv, d], the vec8 window table zhi8).
+    Llama-3.2-3B shape (24 / 8 heads, d 128, theta 5e5), window k=2 and off.
+    Ours reads the same memory as one request of 16-token pages. Each time is
+    the mean of `steps` calls after `warmup`, CUDA events on the stream."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    try:
+        import build_fi_ref
+    finally:
+        sys.path.pop(0)
+    try:
+        mod = build_fi_ref.load()
+    except Exception as e:  # FlashInfer missing or the module does not load here
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    if mod is None:
+        return {"unavailable": "oracle/_ref/fi_atfwin.so was not built (oracle/build_fi_ref.py needs the reference tree)"}
+    from flashinfer.decode import single_decode_with_kv_cache_with_jit_module
+    import atflash
+    from atflash import window_table as WT
+    hq, hkv, page, base = 24, 8, 16, 5e5
+    g = torch.Generator(device=device).manual_seed(1234 + N + D)
+    q = torch.randn((hq, D), generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn((N, hkv, D), generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn((N, hkv, D), generator=g, device=device).to(torch.bfloat16)
+    zhi8 = WT.zhi_slice_vec8(D, base, 2.0, device=device).to(torch.int32)
+    sm = 1.0 / math.sqrt(D)
+
+    def fi(zt):
+        return single_decode_with_kv_cache_with_jit_module(mod, q, k, v, None, zt, 0.0, sm, 1.0, 1e-4)
+
+    def timeit(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps * 1e3
+
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
+    kc, vc = k.view(N // page, page, hkv, D), v.view(N // page, page, hkv, D)
+    indptr = torch.tensor([0, N // page], dtype=torch.int32)
+    idx = torch.arange(N // page, dtype=torch.int32)
+    lpl = torch.tensor([page], dtype=torch.int32)
+    out = torch.empty((1, hq, D), dtype=torch.bfloat16, device=device)
+
+    def ours(wt, mode="snap16"):
+        w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        w.plan(indptr, idx, lpl, hq, hkv, D, page, window_table=wt, window_mode=mode)
+        return lambda: w.run(q[None], (kc, vc), out=out)
+
+    wt = atflash.WindowTable(D, base, 2.0)
+    res = {"shape": f"1 request x {N} keys, {hq}/{hkv} heads, d {D}, theta {base:g}, window k=2",
+           "reference_us": {"on_vec8": timeit(lambda: fi(zhi8)), "off": timeit(lambda: fi(None))},
+           "ours_us": {"on_snap16": timeit(ours(wt)), "on_vec8": timeit(ours(wt, "vec8")), "off": timeit(ours(None))}}
+    # the two kernels compute the same attention: vec8 window against vec8 window
+    ref_on = fi(zhi8)
+    ours(wt, "vec8")()
+    on_diff = (ref_on.float() - out[0].float()).abs().max().item()
+    ref_off = fi(None)
+    ours(None)()
+    off_diff = (ref_off.float() - out[0].float()).abs().max().item()
+    res["max_abs_diff_vs_reference"] = {"on_vec8": on_diff, "off": off_diff}
+    res["speedup_vs_reference"] = {"on": res["reference_us"]["on_vec8"] / res["ours_us"]["on_snap16"],
+                                   "off": res["reference_us"]["off"] / res["ours_us"]["off"]}
+    byts = WT.decode_bytes(hkv, [N], wt.zhi16)["bytes"]
+    res["ours_on_snap16_hbm_frac"] = byts / (res["ours_us"]["on_snap16"] * 1e-6) / 1e9 / peaks["hbm_gbs"]
+    del k, v
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
     """512K-token windowed prefill (k=2), 28/4 heads, zig-zag
     query blocks over the ranks with K/V replicated; max-over-ranks ms."""
@@ -809,10 +889,11 @@ def main():
     ap.add_argument("--impl", default="atflash", choices=["atflash", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip off/k64/decode/e2e/cpu legs")
     ap.add_argument("--only", default="all",
-                    choices=["all", "prefill", "decode", "decode1m", "prefill512k", "request"],
+                    choices=["all", "prefill", "decode", "decode1m", "prefill512k", "request", "refdecode"],
                     help="prefill: the headline leg alone; decode: the config-3 decode leg alone; "
                          "decode1m / prefill512k: the config-5 / config-4 legs alone; request: whole-request "
-                         "on/off timing on a random-weight Qwen2.5-7B-1M-shaped model (1 GPU)")
+                         "on/off timing on a random-weight Qwen2.5-7B-1M-shaped model (1 GPU); refdecode: "
+                         "the reference's FlashInfer window decode beside this repository's (1 GPU)")
     ap.add_argument("--seq-len", type=int, default=131072,
                     help="sequence length (smaller values are for profiling captures)")
     args = ap.parse_args()
@@ -832,6 +913,11 @@ def main():
         res = bench_decode(device, args.steps, args.warmup, peaks, N=args.seq_len)
         if rank == 0:
             print(json.dumps({"decode": res}), flush=True)
+        return
+    if args.only == "refdecode":
+        res = bench_reference_decode_kernel(device, peaks, N=args.seq_len)
+        if rank == 0:
+            print(json.dumps({"refdecode": res}), flush=True)
         return
     if args.only == "request":
         res = bench_request(device, n_ctx=min(args.seq_len, 131072))
@@ -1016,6 +1102,7 @@ def main():
         torch.cuda.empty_cache()
         if world == 1:
             decode = {f"{n // 1024}K": bench_decode(device, 20, 5, peaks, N=n) for n in (8192, 32768, 131072)}
+            decode["reference_kernel_128K"] = bench_reference_decode_kernel(device, peaks)
         decode_1m = bench_decode_1m(device, rank, world, 20, 5, peaks)
         prefill_512k = bench_prefill_512k(device, rank, world, 2, 3, peaks)
     cpu = None
