@@ -48,7 +48,8 @@ class AtfDecodePlanParams(ctypes.Structure):
     _fields_ = [("batch_size", _i32), ("num_qo_heads", _i32), ("num_kv_heads", _i32),
                 ("head_dim", _i32), ("page_size", _i32), ("indptr_host", _vp),
                 ("last_page_len_host", _vp), ("num_sms", _i32), ("min_chunk_keys", _i32),
-                ("max_chunk_keys", _i32)]
+                ("max_chunk_keys", _i32), ("window", ctypes.c_int), ("zhi16", _i32 * 8),
+                ("q_pos_host", _vp), ("kv_pos0_host", _vp)]
 
 
 class AtfDecodePlan(ctypes.Structure):

@@ -67,11 +67,14 @@ class BatchDecodeWithPagedKVCacheWrapper:
              sm_scale: Optional[float] = None, rope_scale=None, rope_theta=None,
              non_blocking: bool = True, *, window_table: Union[None, WindowTable, Sequence[int]] = None,
              window_mode: str = "snap16", qk_layout: str = "sorted_pair",
-             max_chunk_keys: int = 0, min_chunk_keys: int = 0):
+             max_chunk_keys: int = 0, min_chunk_keys: int = 0, q_pos=None, kv_pos0=None):
         """Build the split-KV schedule for a batch of paged requests.
 
         window_table: None (dense), a WindowTable, or a zhi level tuple (snap16).
         qk_layout: pair order of the cached K and of q ("sorted_pair" or "rotate_half").
+        q_pos / kv_pos0: the positions run() will be given (per request; defaults
+        kv_len - 1 and 0). Under a snap16 window the work items are cut to equal
+        bytes read at these distances; they steer the balance only, never the result.
         """
         if pos_encoding_mode != "NONE":
             raise NotImplementedError("RoPE is applied before the cache (pos_encoding_mode NONE)")
@@ -102,17 +105,6 @@ class BatchDecodeWithPagedKVCacheWrapper:
         pp.last_page_len_host = lpl_h.ctypes.data
         pp.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         pp.min_chunk_keys, pp.max_chunk_keys = int(min_chunk_keys), int(max_chunk_keys)
-        plan = _ffi.AtfDecodePlan()
-        lib = _ffi.load()
-        _ffi.check("atf_decode_plan", lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)))
-        items = np.zeros((max(1, plan.num_items), 4), dtype=np.int32)
-        item_indptr = np.zeros(B + 1, dtype=np.int32)
-        _ffi.check("atf_decode_plan", lib.atf_decode_plan(
-            ctypes.byref(pp), items.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), items.shape[0],
-            item_indptr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(plan)))
-        need = 4 * (plan.partial_o_floats + plan.partial_lse_floats) + 256
-        if self._ws.numel() * self._ws.element_size() < need:
-            raise ValueError(f"workspace too small: need {need} bytes")
         # window tables
         zhi16 = [KERNEL_CAP] * 8
         zhi8 = [2 ** 31 - 1] * 16
@@ -137,6 +129,32 @@ class BatchDecodeWithPagedKVCacheWrapper:
                     raise ValueError("zhi levels must be non-negative and non-increasing")
                 zhi16[0] = max(zhi16[0], KERNEL_CAP)
                 mode = _ffi.ATF_WINDOW_SNAP16
+        pp.window = mode
+        for i in range(8):
+            pp.zhi16[i] = zhi16[i]
+        pos_h = []
+        for name, v in (("q_pos", q_pos), ("kv_pos0", kv_pos0)):
+            if v is None:
+                pos_h.append(None)
+                continue
+            a = np.ascontiguousarray((v.detach().cpu().numpy() if isinstance(v, torch.Tensor) else np.asarray(v))
+                                     .astype(np.int64).reshape(-1))
+            if a.shape[0] != B:
+                raise ValueError(f"{name} must have one entry per request")
+            pos_h.append(a)
+        pp.q_pos_host = pos_h[0].ctypes.data if pos_h[0] is not None else None
+        pp.kv_pos0_host = pos_h[1].ctypes.data if pos_h[1] is not None else None
+        plan = _ffi.AtfDecodePlan()
+        lib = _ffi.load()
+        _ffi.check("atf_decode_plan", lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)))
+        items = np.zeros((max(1, plan.num_items), 4), dtype=np.int32)
+        item_indptr = np.zeros(B + 1, dtype=np.int32)
+        _ffi.check("atf_decode_plan", lib.atf_decode_plan(
+            ctypes.byref(pp), items.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), items.shape[0],
+            item_indptr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(plan)))
+        need = 4 * (plan.partial_o_floats + plan.partial_lse_floats) + 256
+        if self._ws.numel() * self._ws.element_size() < need:
+            raise ValueError(f"workspace too small: need {need} bytes")
         kv_lens = [(int(indptr_h[b + 1] - indptr_h[b]) - 1) * page_size + int(lpl_h[b])
                    if indptr_h[b + 1] > indptr_h[b] else 0 for b in range(B)]
         self._plan = {

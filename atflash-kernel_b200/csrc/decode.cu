@@ -23,7 +23,10 @@
 // at global position p has distance z = q_pos - p and reads L(z) levels,
 // L(z) = max(1, #{i : zhi16[i] >= z}); in vec8 mode (sorted-pair layout only)
 // 8-dim slice c is read iff z <= zhi8[c] (kernels/flashinfer_port/fiwin_common.py:35-46).
+#include <limits.h>
 #include <math.h>
+
+#include <vector>
 
 #include "atf_internal.h"
 #include "atf_ptx.cuh"
@@ -151,12 +154,14 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int item = blockIdx.x, hk = blockIdx.y;
   const int b = a.items[4 * item + 0];
-  const int k_beg = a.items[4 * item + 1];
-  const int k_end = a.items[4 * item + 2];
   const int pg0 = a.indptr[b];
   const int npages = a.indptr[b + 1] - pg0;
   const long long kv_len =
       npages > 0 ? static_cast<long long>(npages - 1) * a.page_size + a.last_page_len[b] : 0;
+  // the item's keys, kept inside the request (a plan made for another page
+  // table reads no page outside this request's list)
+  const int k_beg = max(a.items[4 * item + 1], 0);
+  const int k_end = static_cast<int>(min(static_cast<long long>(a.items[4 * item + 2]), kv_len));
   const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
   const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
   const int G = a.G;
@@ -447,6 +452,14 @@ __global__ void __launch_bounds__(THREADS, 2)
       npages > 0 ? static_cast<long long>(npages - 1) * a.page_size + a.last_page_len[b] : 0;
   const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
   const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+  // an item (from atf_decode_plan) starts on a 64-key boundary, lies inside its
+  // request and holds at most MAX_ITEM_KEYS keys (its page list is staged in
+  // shared memory); any other item is reported and skipped
+  if (k_beg < 0 || k_end < k_beg || (k_beg & (STAGE_KEYS - 1)) || k_end > kv_len ||
+      k_end - k_beg > MAX_ITEM_KEYS) {
+    if (tid == 0 && args.err != nullptr) atomicCAS(args.err, 0, kDevErrIndex);
+    return;
+  }
   const int G = a.G;
   const int hq0 = hk * G;
   const int nst = (k_end - k_beg + STAGE_KEYS - 1) / STAGE_KEYS;
@@ -762,60 +775,114 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  // Item size. Every CTA (item, kv head) pays a fixed start-up and drain
-  // cost (barrier set-up, page list, the first loads' latency, the partial
-  // state write), so items are made as long as the occupancy allows: the
-  // CTAs are kept within the fewest full waves of 2 resident CTAs per SM
-  // that the longest allowed item (16384 keys, the page list staged in shared
-  // memory) permits, and within that the items are cut as finely as the waves
-  // hold (the most even split). Keys are cut in multiples of 64 (a stage).
+  if (p->window == ATF_WINDOW_SNAP16)
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i)
+      if (p->zhi16[i] < 0 || (i > 0 && p->zhi16[i] > p->zhi16[i - 1])) return ATF_ERR_INVALID_ARG;
+  // Item sizes. Every CTA (item, kv head) pays a fixed start-up and drain cost
+  // (barrier set-up, page list, the first loads' latency, the partial state
+  // write), so items are made as long as the occupancy allows: the CTAs are
+  // kept within the fewest full waves of 2 resident CTAs per SM that the
+  // longest allowed item (16384 keys, the page list staged in shared memory)
+  // permits. Within that, the items are cut as finely as the waves hold and to
+  // equal cost, so that no CTA of the last wave runs much longer than the
+  // others. The cost of a key is the bytes its CTA reads for it, in 32-byte
+  // units: 8 for the V row plus one per in-window K level. Under a window, a
+  // key far from the query costs 9-12 units and a near one up to 16, so equal
+  // key counts would leave the CTAs nearest the query the slowest. Cuts fall on
+  // multiples of 64 keys (a stage).
   const long long slots = 2ll * sms;
   const long long min_chunk = p->min_chunk_keys > 0 ? p->min_chunk_keys : 256;
   long long cap = decode_tma::MAX_ITEM_KEYS;
   if (p->max_chunk_keys > 0 && p->max_chunk_keys < cap) cap = p->max_chunk_keys;
   cap = cap / 64 * 64;
   if (cap < 64) cap = 64;
+  const bool by_bytes = p->window == ATF_WINDOW_SNAP16;
+  struct Req {
+    long long len, total;
+    long long lim[ATF_MAX_LEVELS];  // K level i is read by local keys n >= lim[i]
+  };
+  std::vector<Req> reqs(static_cast<size_t>(p->batch_size));
+  // cost of the local keys [n0, n1) of a request
+  auto cost = [](const Req& r, long long n0, long long n1) {
+    long long c = 8 * (n1 - n0);
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i) {
+      const long long lo = n0 > r.lim[i] ? n0 : r.lim[i];
+      if (n1 > lo) c += n1 - lo;
+    }
+    return c;
+  };
+  for (int b = 0; b < p->batch_size; ++b) {
+    Req& r = reqs[static_cast<size_t>(b)];
+    const int np = p->indptr_host[b + 1] - p->indptr_host[b];
+    r.len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + p->last_page_len_host[b] : 0;
+    const long long q_pos = p->q_pos_host != nullptr ? p->q_pos_host[b] : r.len - 1;
+    const long long pos0 = p->kv_pos0_host != nullptr ? p->kv_pos0_host[b] : 0;
+    // a key at distance z = q_pos - (pos0 + n) reads level i when z <= zhi16[i];
+    // level 0 is always read
+    for (int i = 0; i < ATF_MAX_LEVELS; ++i)
+      r.lim[i] = (!by_bytes || i == 0) ? LLONG_MIN / 4 : q_pos - pos0 - static_cast<long long>(p->zhi16[i]);
+    r.total = cost(r, 0, r.len);
+  }
+  // pieces of request r under the per-item cost bound c
+  auto pieces = [&](const Req& r, long long c) -> long long {
+    if (r.len == 0) return 0;
+    const long long m_lo = (r.len + cap - 1) / cap;
+    long long m_hi = r.len / min_chunk;
+    if (m_hi < m_lo) m_hi = m_lo;
+    long long m = (r.total + c - 1) / c;
+    return m < m_lo ? m_lo : (m > m_hi ? m_hi : m);
+  };
   auto ctas_for = [&](long long c) {
     long long n = 0;
-    for (int b = 0; b < p->batch_size; ++b) {
-      const int np = p->indptr_host[b + 1] - p->indptr_host[b];
-      const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + p->last_page_len_host[b] : 0;
-      n += (len + c - 1) / c;
-    }
+    for (const Req& r : reqs) n += pieces(r, c);
     return n * p->num_kv_heads;
   };
-  const long long waves = (ctas_for(cap) + slots - 1) / slots;
-  long long chunk = cap;
-  // the smallest chunk (most CTAs) that still fits in `waves` full waves
-  long long lo = (min_chunk + 63) / 64 * 64, hi = cap;
-  if (lo > hi) lo = hi;
-  while (lo < hi) {
-    const long long mid = (lo + hi) / 2 / 64 * 64;
-    if (mid < lo) break;
-    if (ctas_for(mid) <= waves * slots) hi = mid; else lo = mid + 64;
+  long long c_hi = 1;
+  for (const Req& r : reqs) c_hi = r.total > c_hi ? r.total : c_hi;
+  const long long waves = (ctas_for(c_hi) + slots - 1) / slots;
+  // the smallest cost bound (most CTAs) that still fits in `waves` full waves
+  long long c_lo = 1;
+  while (c_lo < c_hi) {
+    const long long mid = c_lo + (c_hi - c_lo) / 2;
+    if (ctas_for(mid) <= waves * slots) c_hi = mid; else c_lo = mid + 1;
   }
-  // the smallest such chunk also splits each request most evenly
-  chunk = hi;
-  if (chunk < 64) chunk = 64;
   int n = 0;
+  long long longest = 0;
   for (int b = 0; b < p->batch_size; ++b) {
-    const int np = p->indptr_host[b + 1] - p->indptr_host[b];
-    const long long len = np > 0 ? static_cast<long long>(np - 1) * p->page_size + p->last_page_len_host[b] : 0;
+    const Req& r = reqs[static_cast<size_t>(b)];
+    const long long m = pieces(r, c_hi);
     if (item_indptr_host != nullptr) item_indptr_host[b] = n;
-    for (long long k0 = 0; k0 < len; k0 += chunk) {
+    // piece j ends at the first 64-key boundary where the running cost reaches
+    // (j + 1) / m of the request's; no piece is empty or longer than `cap`
+    long long n0 = 0;
+    for (long long j = 0; n0 < r.len; ++j) {
+      long long n1 = r.len;
+      if (j + 1 < m) {
+        const long long target = (r.total * (j + 1) + m - 1) / m;
+        long long ulo = n0 / 64 + 1, uhi = (r.len + 63) / 64;
+        while (ulo < uhi) {
+          const long long mid = ulo + (uhi - ulo) / 2;
+          const long long e = mid * 64 < r.len ? mid * 64 : r.len;
+          if (cost(r, 0, e) >= target) uhi = mid; else ulo = mid + 1;
+        }
+        n1 = ulo * 64 < r.len ? ulo * 64 : r.len;
+      }
+      if (n1 - n0 > cap) n1 = n0 + cap;
       if (items_host != nullptr) {
         if (n >= items_capacity) return ATF_ERR_WORKSPACE;
         items_host[4 * n + 0] = b;
-        items_host[4 * n + 1] = static_cast<int32_t>(k0);
-        items_host[4 * n + 2] = static_cast<int32_t>(k0 + chunk < len ? k0 + chunk : len);
+        items_host[4 * n + 1] = static_cast<int32_t>(n0);
+        items_host[4 * n + 2] = static_cast<int32_t>(n1);
         items_host[4 * n + 3] = 0;
       }
+      longest = n1 - n0 > longest ? n1 - n0 : longest;
+      n0 = n1;
       ++n;
     }
   }
   if (item_indptr_host != nullptr) item_indptr_host[p->batch_size] = n;
   out->num_items = n;
-  out->chunk_keys = static_cast<int32_t>(chunk);
+  out->chunk_keys = static_cast<int32_t>(longest);
   out->partial_o_floats = static_cast<int64_t>(n) * p->num_qo_heads * ATF_HEAD_DIM;
   out->partial_lse_floats = static_cast<int64_t>(n) * p->num_qo_heads;
   return ATF_OK;

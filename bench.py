@@ -536,13 +536,14 @@ def bench_decode(device, steps, warmup, peaks, N=131072):
     indptr = torch.arange(0, total + 1, npg, dtype=torch.int32)
     lpl = torch.full((B,), page, dtype=torch.int32)
     ws = torch.empty(128 * 1024 * 1024, dtype=torch.uint8, device=device)
-    # the same K pages laid out level-major (P, Hkv, 8, page, 16): a page's
-    # in-window levels are one contiguous run
-    kc_lm = kc.view(total, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous()
+    # the cache as this framework keeps it: level-major K pages (P, Hkv, 8, page,
+    # 16), in which a page's in-window levels are one contiguous run; the NHD K
+    # pages of FlashInfer's layout are timed beside it
+    kc_lm = level_major(kc)
     res = {}
-    for name, wt, kk in (("on", atflash.WindowTable(D, 5e5, 2.0), kc), ("off", None, kc),
-                         ("on_level_major_k", atflash.WindowTable(D, 5e5, 2.0), kc_lm),
-                         ("off_level_major_k", None, kc_lm)):
+    for name, wt, kk in (("on", atflash.WindowTable(D, 5e5, 2.0), kc_lm), ("off", None, kc_lm),
+                         ("on_nhd_k", atflash.WindowTable(D, 5e5, 2.0), kc),
+                         ("off_nhd_k", None, kc)):
         w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
         w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt)
         out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=device)
@@ -552,8 +553,8 @@ def bench_decode(device, steps, warmup, peaks, N=131072):
         res[name] = {"us": ms * 1e3, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9}
     res["ratio_on_off"] = res["off"]["us"] / res["on"]["us"]
     res["hbm_frac_on"] = res["on"]["gbs"] / peaks["hbm_gbs"]
-    res["ratio_on_off_level_major_k"] = res["off_level_major_k"]["us"] / res["on_level_major_k"]["us"]
-    res["hbm_frac_on_level_major_k"] = res["on_level_major_k"]["gbs"] / peaks["hbm_gbs"]
+    res["ratio_on_off_nhd_k"] = res["off_nhd_k"]["us"] / res["on_nhd_k"]["us"]
+    res["hbm_frac_on_nhd_k"] = res["on_nhd_k"]["gbs"] / peaks["hbm_gbs"]
     del kc, vc, kc_lm
     torch.cuda.empty_cache()
     return res
@@ -582,11 +583,16 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
     q_pos = torch.tensor([N - 1], dtype=torch.int64, device=device)
     kv_pos0 = torch.tensor([rank * shard], dtype=torch.int64, device=device)
     ws = torch.empty(64 * 1024 * 1024, dtype=torch.uint8, device=device)
+    # the cache as this framework keeps it: level-major K pages (each 16-dim
+    # level of a page one contiguous run, written so by atf_paged_kv_append),
+    # NHD V pages. The NHD K copy is timed beside it (window on only).
+    kc_lm = level_major(kc)
     res = {}
-    for name, wt in (("on_k64", atflash.WindowTable(D, THETA, 64.0)), ("off", None)):
+    for name, wt, kk in (("on_k64", atflash.WindowTable(D, THETA, 64.0), kc_lm), ("off", None, kc_lm),
+                         ("on_k64_nhd_k", atflash.WindowTable(D, THETA, 64.0), kc)):
         w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
-        w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt)
-        ms, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0),
+        w.plan(indptr, perm, lpl, hq, hkv, D, page, window_table=wt, q_pos=q_pos, kv_pos0=kv_pos0)
+        ms, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0),
                       steps, warmup, world)
         zhi = wt.zhi16 if wt is not None else None
         mine = WT.decode_bytes(hkv, [shard], zhi, q_pos=[N - 1 - rank * shard])["bytes"]
@@ -597,9 +603,11 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
         agg = total / (ms * 1e-3) / 1e9
         res[name] = {"us": ms * 1e3, "bytes_total": total, "gbs_aggregate": agg,
                      "hbm_frac_per_gpu": agg / (world * peaks["hbm_gbs"])}
+        if kk is kc:
+            continue
         # the same step from atflash.dist.ShardedDecodeStep: the rank's decode and the
         # cross-rank merge replay as CUDA graphs, the all-gather runs eagerly between
-        step = atflash.dist.ShardedDecodeStep(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0)
+        step = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0)
         ms_g, _ = timed(lambda i: step(), steps, warmup, world)
         step.release()
         res[name]["us_graph"] = ms_g * 1e3
@@ -609,9 +617,9 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
             # (atflash.dist.StateExchange) instead of the NCCL all-gather: eager,
             # and the whole step replayed from one CUDA graph
             ex = atflash.dist.StateExchange(B, hq)
-            ms_x, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0,
+            ms_x, _ = timed(lambda i: atflash.dist.sharded_decode(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0,
                                                                   exchange=ex), steps, warmup, world)
-            xstep = atflash.dist.ShardedDecodeStep(q, w, (kc, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
+            xstep = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
             ms_xg, _ = timed(lambda i: xstep(), steps, warmup, world)
             xstep.release()
             barrier(world)
@@ -621,14 +629,24 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
             res[name]["us_exchange_graph"] = ms_xg * 1e3
             res[name]["gbs_aggregate_exchange_graph"] = total / (ms_xg * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
-    res["parity"] = decode_1m_parity(device, rank, world, q, (kc, vc), perm, q_pos, kv_pos0, N, shard, page)
-    res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, KV split into {world} shards, "
+    res["parity"] = decode_1m_parity(device, rank, world, q, (kc, vc), kc_lm, perm, q_pos, kv_pos0, N, shard,
+                                     page)
+    res["config"] = (f"1 request x {N} keys, 28/4 heads, page {page}, level-major K pages (on_k64_nhd_k: "
+                     f"NHD K pages), KV split into {world} shards, "
                      "all-gather of (O, LSE) + LSE merge inside the step; us: eager "
                      "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep; us_exchange(_graph): "
                      "the states exchanged by NVLink peer stores (atflash.dist.StateExchange), no collective")
-    del kc, vc
+    del kc, vc, kc_lm
     torch.cuda.empty_cache()
     return res
+
+
+def level_major(kc):
+    """NHD K pages (P, page, Hkv, 128) as level-major pages (P, Hkv, 8, page, 16):
+    the layout atf_paged_kv_append writes with k_level_major, in which a page's
+    in-window levels are one contiguous run per level."""
+    P, page, hkv, _ = kc.shape
+    return kc.view(P, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous()
 
 
 def _decode_1m_shard(device, r, shard, page, hkv):
@@ -642,7 +660,7 @@ def _decode_1m_shard(device, r, shard, page, hkv):
     return kc, vc, perm
 
 
-def decode_1m_parity(device, rank, world, q, cache, perm, q_pos, kv_pos0, N, shard, page):
+def decode_1m_parity(device, rank, world, q, cache, k_lm, perm, q_pos, kv_pos0, N, shard, page):
     """Correctness of the config-5 step, checked inside the bench run, window
     k=64 and off. One rank: q heads 0-6 (kv head 0) against the numpy oracle
     (ref_window_attn phase="decode", every key). Several ranks: rank 0 decodes
@@ -658,8 +676,8 @@ def decode_1m_parity(device, rank, world, q, cache, perm, q_pos, kv_pos0, N, sha
         ws = torch.empty(64 * 1024 * 1024, dtype=torch.uint8, device=device)
         w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
         w.plan(torch.tensor([0, shard // page], dtype=torch.int32), perm, torch.tensor([page], dtype=torch.int32),
-               hq, hkv, D, page, window_table=wt)
-        o, l = atflash.dist.sharded_decode(q, w, cache, q_pos=q_pos, kv_pos0=kv_pos0)
+               hq, hkv, D, page, window_table=wt, q_pos=q_pos, kv_pos0=kv_pos0)
+        o, l = atflash.dist.sharded_decode(q, w, (k_lm, cache[1]), q_pos=q_pos, kv_pos0=kv_pos0)
         torch.cuda.synchronize()
         if rank == 0 and world == 1:
             from oracle import attention as OA
@@ -681,8 +699,9 @@ def decode_1m_parity(device, rank, world, q, cache, perm, q_pos, kv_pos0, N, sha
                     device, r, shard, page, hkv)
                 w_r = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
                 w_r.plan(torch.tensor([0, shard // page], dtype=torch.int32), perm_r,
-                         torch.tensor([page], dtype=torch.int32), hq, hkv, D, page, window_table=wt)
-                o_r, l_r = w_r.run(q, (kc_r, vc_r), q_pos=q_pos,
+                         torch.tensor([page], dtype=torch.int32), hq, hkv, D, page, window_table=wt,
+                         q_pos=[N - 1], kv_pos0=[r * shard])
+                o_r, l_r = w_r.run(q, (level_major(kc_r) if r else k_lm, vc_r), q_pos=q_pos,
                                    kv_pos0=torch.tensor([r * shard], dtype=torch.int64, device=device),
                                    return_lse=True, out_dtype=torch.float32)
                 po.append(o_r)
@@ -825,15 +844,20 @@ def bench_reference_decode_kernel(device, peaks, N=131072, steps=50, warmup=10):
     lpl = torch.tensor([page], dtype=torch.int32)
     out = torch.empty((1, hq, D), dtype=torch.bfloat16, device=device)
 
-    def ours(wt, mode="snap16"):
+    kc_lm = level_major(kc)
+
+    def ours(wt, mode="snap16", kk=kc):
         w = atflash.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
         w.plan(indptr, idx, lpl, hq, hkv, D, page, window_table=wt, window_mode=mode)
-        return lambda: w.run(q[None], (kc, vc), out=out)
+        return lambda: w.run(q[None], (kk, vc), out=out)
 
     wt = atflash.WindowTable(D, base, 2.0)
-    res = {"shape": f"1 request x {N} keys, {hq}/{hkv} heads, d {D}, theta {base:g}, window k=2",
+    res = {"shape": f"1 request x {N} keys, {hq}/{hkv} heads, d {D}, theta {base:g}, window k=2; ours reads "
+                    "the same K/V memory as 16-token NHD pages, and (*_level_major_k) a level-major copy of K",
            "reference_us": {"on_vec8": timeit(lambda: fi(zhi8)), "off": timeit(lambda: fi(None))},
-           "ours_us": {"on_snap16": timeit(ours(wt)), "on_vec8": timeit(ours(wt, "vec8")), "off": timeit(ours(None))}}
+           "ours_us": {"on_snap16": timeit(ours(wt)), "on_vec8": timeit(ours(wt, "vec8")), "off": timeit(ours(None)),
+                       "on_snap16_level_major_k": timeit(ours(wt, kk=kc_lm)),
+                       "off_level_major_k": timeit(ours(None, kk=kc_lm))}}
     # the two kernels compute the same attention: vec8 window against vec8 window
     ref_on = fi(zhi8)
     ours(wt, "vec8")()
@@ -846,7 +870,7 @@ def bench_reference_decode_kernel(device, peaks, N=131072, steps=50, warmup=10):
                                    "off": res["reference_us"]["off"] / res["ours_us"]["off"]}
     byts = WT.decode_bytes(hkv, [N], wt.zhi16)["bytes"]
     res["ours_on_snap16_hbm_frac"] = byts / (res["ours_us"]["on_snap16"] * 1e-6) / 1e9 / peaks["hbm_gbs"]
-    del k, v
+    del k, v, kc_lm
     torch.cuda.empty_cache()
     return res
 

@@ -140,18 +140,29 @@ typedef struct {
   int32_t num_sms;        /* 0: query the current device */
   int32_t min_chunk_keys; /* 0: default (256) */
   int32_t max_chunk_keys; /* 0: unlimited; forces at least ceil(len/max) splits */
+  /* Optional window of the run (ATF_WINDOW_SNAP16 with its zhi16 table): the
+   * items are then cut to equal bytes read (V rows plus in-window K levels)
+   * instead of equal key counts. OFF / VEC8: equal key counts. q_pos_host and
+   * kv_pos0_host (optional, [batch], host) give the positions the run will use
+   * (defaults kv_len-1 and 0); they only steer the balance, never the result. */
+  int32_t window;
+  int32_t zhi16[ATF_MAX_LEVELS];
+  const int64_t* q_pos_host;
+  const int64_t* kv_pos0_host;
 } AtfDecodePlanParams;
 
 typedef struct {
   int32_t num_items;       /* work items (request, key range) */
-  int32_t chunk_keys;      /* keys per item (multiple of 64) */
+  int32_t chunk_keys;      /* keys of the longest item */
   int64_t partial_o_floats;   /* workspace floats needed for partial outputs */
   int64_t partial_lse_floats; /* workspace floats needed for partial LSEs */
 } AtfDecodePlan;
 
 /* Build the split-KV schedule on the host. items_host receives num_items rows
  * of int32[4] = {request, key_begin, key_end, 0}; item_indptr_host receives
- * batch+1 offsets. Pass NULL buffers to query sizes only. */
+ * batch+1 offsets. Pass NULL buffers to query sizes only. Items start on
+ * multiples of 64 keys and hold at most 16384 keys (atf_decode_run's kernels
+ * report longer or unaligned items through error_flag and skip them). */
 int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host, int32_t items_capacity,
                     int32_t* item_indptr_host, AtfDecodePlan* out);
 

@@ -13,6 +13,7 @@ prefill, every row of sampled 128-row query tiles for sampled heads.
   config 5  one 1M-key request, 28/4 heads, page 64, theta 1e7, window k=64 and
             off; also the KV sequence cut into 4 shards with global positions
             and merged by LSE (the single-GPU emulation of the 4-GPU step)
+  (decode)  the same cache with level-major K pages gives bit-identical output
   config 2  128K prefill, 28/4 heads, theta 1e7, window k=2, k=64 and off
 
 Pass bar: max |err| <= 2e-2 and mean |err| <= 2e-3 against the fp32 oracle."""
@@ -52,6 +53,13 @@ def _request_head(kc, vc, perm, indptr, b, hk, N):
     return k.float().cpu().numpy(), v.float().cpu().numpy()
 
 
+def _level_major(kc):
+    """The same K pages level-major, (P, Hkv, 8, page, 16): the cache layout
+    atf_paged_kv_append writes with k_level_major."""
+    P, page, hkv, _ = kc.shape
+    return kc.view(P, page, hkv, 8, 16).permute(0, 2, 3, 1, 4).contiguous()
+
+
 def _oracle_decode_group(q_group, k, v, w):
     """ref_window_attn(phase="decode", block_m=1, block_n=1) for the G query
     heads of one kv head: q_group (G, d), k/v (N, d) -> (G, d)."""
@@ -81,7 +89,11 @@ def test_decode_config3(cuda_device, N):
     q, kc, vc, indptr, perm, lpl = _paged_device_cache(cuda_device, B, N, hq, hkv, page, 1234 + N + D)
     for k_ret in (2.0, None):
         wt = atflash.WindowTable(D, base, k_ret) if k_ret is not None else None
-        out = _run_decode(cuda_device, q, kc, vc, indptr, perm, lpl, hq, hkv, page, wt).float().cpu().numpy()
+        out_t = _run_decode(cuda_device, q, kc, vc, indptr, perm, lpl, hq, hkv, page, wt)
+        # level-major K pages hold the same values: the same bits out
+        out_lm = _run_decode(cuda_device, q, _level_major(kc), vc, indptr, perm, lpl, hq, hkv, page, wt)
+        assert torch.equal(out_lm.view(torch.int16), out_t.view(torch.int16)), k_ret
+        out = out_t.float().cpu().numpy()
         w = OWT.wavelengths_sorted(D, base, float("inf") if k_ret is None else k_ret)
         for b in (0, B - 1):
             for hk in (0, 3, hkv - 1):
@@ -105,6 +117,9 @@ def test_decode_config5_1m(cuda_device):
     for k_ret in (64.0, None):
         wt = atflash.WindowTable(D, base, k_ret) if k_ret is not None else None
         out = _run_decode(cuda_device, q, kc, vc, indptr, perm, lpl, hq, hkv, page, wt)
+        out_lm = _run_decode(cuda_device, q, _level_major(kc), vc, indptr, perm, lpl, hq, hkv, page, wt)
+        assert torch.equal(out_lm.view(torch.int16), out.view(torch.int16)), k_ret
+        del out_lm
         w = OWT.wavelengths_sorted(D, base, float("inf") if k_ret is None else k_ret)
         outn = out.float().cpu().numpy()
         for hk in (0, hkv - 1):

@@ -152,6 +152,11 @@ def _plan(lib, lens, page, hq=24, hkv=8, **kw):
     pp.indptr_host, pp.last_page_len_host = indptr.ctypes.data, lpl.ctypes.data
     pp.num_sms = kw.get("sms", 148)
     pp.max_chunk_keys = kw.get("max_chunk", 0)
+    zhi = kw.get("zhi")
+    if zhi is not None:
+        pp.window = _ffi.ATF_WINDOW_SNAP16
+        for i in range(8):
+            pp.zhi16[i] = zhi[i]
     plan = _ffi.AtfDecodePlan()
     assert lib.atf_decode_plan(ctypes.byref(pp), None, 0, None, ctypes.byref(plan)) == 0
     items = np.zeros((max(1, plan.num_items), 4), dtype=np.int32)
@@ -162,19 +167,57 @@ def _plan(lib, lens, page, hq=24, hkv=8, **kw):
     return plan, items[:plan.num_items], iptr
 
 
-@pytest.mark.parametrize("lens,page", [([131072] * 8, 16), ([8192, 1, 70000], 16), ([1048576], 64), ([5], 1)])
-def test_decode_plan_covers_every_key_once(lens, page):
+_ZHI_K2 = (2147483647, 992572, 192482, 37326, 7238, 1403, 272, 52)  # theta 5e5, k = 2
+
+
+@pytest.mark.parametrize("zhi", [None, _ZHI_K2])
+@pytest.mark.parametrize("lens,page", [([131072] * 8, 16), ([8192, 1, 70000], 16), ([1048576], 64), ([5], 1),
+                                       ([0, 300, 0], 16)])
+def test_decode_plan_covers_every_key_once(lens, page, zhi):
     lib = _lib()
-    plan, items, iptr = _plan(lib, lens, page)
-    assert plan.chunk_keys % 64 == 0
+    plan, items, iptr = _plan(lib, lens, page, zhi=zhi)
+    assert plan.chunk_keys == max([int(k1 - k0) for (_, k0, k1, _) in items] + [0])
     for b, n in enumerate(lens):
         its = items[iptr[b]:iptr[b + 1]]
         assert its[:, 0].tolist() == [b] * len(its)
         cover = np.zeros(n, dtype=np.int32)
         for (_, k0, k1, _) in its:
+            assert k0 % 64 == 0 and 0 < k1 - k0 <= 16384
             cover[k0:k1] += 1
         assert (cover == 1).all()
     assert plan.partial_o_floats == plan.num_items * 24 * 128
+
+
+def _item_bytes(items, lens, zhi):
+    """Bytes one kv head's CTA reads for each item: V rows plus the in-window
+    K levels of every key (a key at distance z reads max(1, #{zhi[i] >= z}))."""
+    out = []
+    for (b, k0, k1, _) in items:
+        z = lens[b] - 1 - np.arange(k0, k1)
+        levels = np.maximum(1, (np.asarray(zhi)[None, :] >= z[:, None]).sum(1))
+        out.append(int((256 + 32 * levels).sum()))
+    return np.array(out)
+
+
+@pytest.mark.parametrize("lens,page,hkv", [([131072] * 8, 16, 8), ([1048576], 64, 4), ([200000, 9000], 16, 8)])
+def test_decode_plan_balances_window_bytes(lens, page, hkv):
+    """Under a snap16 window the items of a request carry equal bytes (to a
+    64-key stage), not equal key counts: far keys read fewer K levels, so the
+    items far from the query are longer."""
+    lib = _lib()
+    _, items, iptr = _plan(lib, lens, page, hkv=hkv, zhi=_ZHI_K2)
+    for b in range(len(lens)):
+        its = items[iptr[b]:iptr[b + 1]]
+        if len(its) < 2:
+            continue
+        c = _item_bytes(its, lens, _ZHI_K2)
+        # each cut falls on a stage boundary: within two stages of the densest keys
+        assert c.max() - c.min() <= 2 * 64 * 512
+        keys = its[:, 2] - its[:, 1]
+        assert keys[0] >= keys[-1]  # the oldest keys are the cheapest
+    _, even, _ = _plan(lib, lens, page, hkv=hkv)
+    # the same number of CTAs as the unwindowed plan
+    assert len(items) == len(even)
 
 
 def test_decode_plan_rejects_bad_tables():
