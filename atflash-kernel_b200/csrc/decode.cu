@@ -72,25 +72,40 @@ __device__ __forceinline__ int level_of_chunk(int layout, int c) {
   return layout == ATF_LAYOUT_SORTED_PAIR ? (c >> 1) : 7 - (c & 7);
 }
 
-__device__ __forceinline__ int levels_at(const Args& a, long long z) {
-  if (a.window == ATF_WINDOW_OFF) return 8;
+// The window as limits on local key indices, computed once per CTA and kept in
+// registers: a key of local index n is at distance z = zb - n (zb = q_pos -
+// kv_pos0) and reads a level or chunk whose zhi is >= z, i.e. when n >= zb - zhi.
+// Per-key level counts are then 32-bit compares against registers; evaluating
+// 64-bit distances against the table in the kernel parameters for every key
+// group took most of a consumer warp's time per stage.
+__device__ __forceinline__ int key_limit(long long zb, long long zhi) {
+  const long long v = zb - zhi;
+  return static_cast<int>(v < INT_MIN ? INT_MIN : (v > INT_MAX ? INT_MAX : v));
+}
+// level i (0..7): snap16, L(z) = max(1, #{i : zhi16[i] >= z}) (zhi16 is
+// non-increasing, so level 0 always and level i when zhi16[i] >= z); vec8, a
+// level when its first (wider) slice is read; every level when the window is off
+__device__ __forceinline__ int level_limit(const Args& a, long long zb, int i) {
+  if (a.window == ATF_WINDOW_OFF) return INT_MIN;
+  if (a.window == ATF_WINDOW_SNAP16) return i == 0 ? INT_MIN : key_limit(zb, a.zhi16[i]);
+  return key_limit(zb, a.zhi8[2 * i]);
+}
+// 16-byte chunk c of a K row: snap16, when its level is read; vec8, when its
+// 8-dim slice is read (zhi8[c] >= z)
+__device__ __forceinline__ int chunk_limit(const Args& a, long long zb, int c) {
+  if (a.window == ATF_WINDOW_OFF) return INT_MIN;
   if (a.window == ATF_WINDOW_SNAP16) {
-    int L = 0;
-#pragma unroll
-    for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi16[i]) >= z) ? 1 : 0;
-    return L < 1 ? 1 : L;
+    const int l = level_of_chunk(a.layout, c);
+    return l == 0 ? INT_MIN : key_limit(zb, a.zhi16[l]);
   }
-  // vec8: a level is needed when its first (wider) slice is active.
+  return key_limit(zb, a.zhi8[c]);
+}
+// levels read by local key n
+__device__ __forceinline__ int levels_of(const int (&lim)[ATF_MAX_LEVELS], int n) {
   int L = 0;
 #pragma unroll
-  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi8[2 * i]) >= z) ? 1 : 0;
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += n >= lim[i] ? 1 : 0;
   return L;
-}
-
-__device__ __forceinline__ bool chunk_active(const Args& a, int c, long long z) {
-  if (a.window == ATF_WINDOW_OFF) return true;
-  if (a.window == ATF_WINDOW_SNAP16) return level_of_chunk(a.layout, c) < levels_at(a, z);
-  return static_cast<long long>(a.zhi8[c]) >= z;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
@@ -117,6 +132,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
+}
+// Transpose of an 8x8 b16 matrix held one row pair per thread (the mma
+// fragment layout): lane (g, t4) gets elements (2 t4, g) and (2 t4 + 1, g).
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
+  return d;
 }
 // D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -166,6 +188,10 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
   const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
   const int G = a.G;
   const int hq0 = hk * G;
+  int lim[ATF_MAX_LEVELS];
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = level_limit(a, q_pos - pos0, i);
+  const int klim = chunk_limit(a, q_pos - pos0, tid & 15);  // this thread's K chunk
 
   // Q fragments (A operand): rows = heads g / g+8 of the group, K = the 16 dims
   // of each level (first 8 from half 0, next 8 from half 1 of the level).
@@ -205,8 +231,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
       const long long off = static_cast<long long>(page) * a.s_page +
                             static_cast<long long>(nn % a.page_size) * a.s_tok +
                             static_cast<long long>(hk) * a.s_head + c * 8;
-      const long long z = q_pos - (pos0 + n);
-      cp_async16(kb + sw_off(row, c), a.kc + off, valid && chunk_active(a, c, z));
+      cp_async16(kb + sw_off(row, c), a.kc + off, valid && n >= klim);
       cp_async16(vb + sw_off(row, c), a.vc + off, valid);
     }
   };
@@ -235,7 +260,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
     const int key0 = k_beg + s * KEYS_PER_STAGE + warp * 16;  // first key of this warp
     if (key0 < k_end) {
       const int last = (key0 + 15 < k_end ? key0 + 15 : k_end - 1);
-      const int Lmax = levels_at(a, q_pos - (pos0 + last));
+      const int Lmax = levels_of(lim, last);
       float sc[2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
@@ -418,14 +443,14 @@ struct KMaps {
   CUtensorMap lv[ATF_MAX_LEVELS];
 };
 
-__device__ __forceinline__ int snap_levels(const decode::Args& a, long long z) {
-  if (a.window == ATF_WINDOW_OFF) return 8;
-  int L = 0;
-#pragma unroll
-  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi16[i]) >= z) ? 1 : 0;
-  return L < 1 ? 1 : L;
-}
 
+// KR (keys as MMA rows, for GQA groups of at most 8 query heads): S^T = K Q^T
+// as m16n8k16 with the 16 keys of a warp's group as rows and the group's heads
+// as the 8 columns, one MMA per in-window level; P^T is moved into the B
+// operand with movmatrix and O^T += V^T P^T takes one MMA per 16 dims. The
+// heads-as-rows form (!KR, any group up to 16) pads the G heads to 16 MMA rows
+// and needs twice the MMAs.
+template <bool KR>
 __global__ void __launch_bounds__(THREADS, 2)
     decode_tma_kernel(const __grid_constant__ KMaps tmK, const __grid_constant__ CUtensorMap tmV,
                       const Args args) {
@@ -463,8 +488,11 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int G = a.G;
   const int hq0 = hk * G;
   const int nst = (k_end - k_beg + STAGE_KEYS - 1) / STAGE_KEYS;
+  int lim[ATF_MAX_LEVELS];
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, q_pos - pos0, i);
   // ring geometry of this item (the same in every role)
-  const int Lc = k_end > k_beg ? snap_levels(a, q_pos - (pos0 + k_end - 1)) : ATF_MAX_LEVELS;
+  const int Lc = k_end > k_beg ? decode::levels_of(lim, k_end - 1) : ATF_MAX_LEVELS;
   const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
   const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
   const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
@@ -481,11 +509,14 @@ __global__ void __launch_bounds__(THREADS, 2)
   const AbortCtl ab{s_abort, args.err};
   const bool start_ok = (*s_abort == 0);
 
+  // KR: heads 2 t4 and 2 t4 + 1 of the group (l_run: this thread's keys only);
+  // otherwise rows g and g + 8
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
-  float o[16][4];
+  constexpr int OT = KR ? 8 : 16;  // O fragments: 16 dims x 8 heads / 16 heads x 8 dims
+  float o[OT][4];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   const int g = lane >> 2, t4 = lane & 3;
 
   if (start_ok && warp == CONSUMERS) {
@@ -514,7 +545,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       int L = 0;
       if (live) {
         const int n_last = min(k0 + r0 + R, k_end) - 1;
-        L = snap_levels(a, q_pos - (pos0 + n_last));
+        L = decode::levels_of(lim, n_last);
       }
       // bytes: sum over slices (the K lanes carry them)
       uint32_t my_bytes = (live && !is_v) ? static_cast<uint32_t>(R) * (32u * L + 256u) : 0u;
@@ -545,19 +576,33 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
   } else if (start_ok) {
     // ------------------------------------------------------------ consumers
-    uint32_t qa[8][4];
-    {
-      const __nv_bfloat16* qrow0 =
+    // Q fragments of the group (level i = dims 16i..16i+15, sorted-pair): KR as
+    // the B operand (heads as columns), else as the A operand (heads as rows)
+    uint32_t qa[KR ? 1 : 8][4];
+    uint32_t qb[KR ? 8 : 1][2];
+    if constexpr (KR) {
+      const __nv_bfloat16* qrow =
           a.q + static_cast<long long>(b) * a.q_sb + static_cast<long long>(hq0 + g) * a.q_sh;
-      const __nv_bfloat16* qrow1 = qrow0 + 8 * a.q_sh;
-      const bool v0 = g < G, v1 = g + 8 < G;
+      const bool v0 = g < G;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int c0 = 16 * i + 2 * t4, c1 = 16 * i + 8 + 2 * t4;
-        qa[i][0] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0) : 0u;
-        qa[i][1] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0) : 0u;
-        qa[i][2] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c1) : 0u;
-        qa[i][3] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c1) : 0u;
+        qb[i][0] = v0 ? *reinterpret_cast<const uint32_t*>(qrow + 16 * i + 2 * t4) : 0u;
+        qb[i][1] = v0 ? *reinterpret_cast<const uint32_t*>(qrow + 16 * i + 8 + 2 * t4) : 0u;
+      }
+    } else {
+      {
+        const __nv_bfloat16* qrow0 =
+            a.q + static_cast<long long>(b) * a.q_sb + static_cast<long long>(hq0 + g) * a.q_sh;
+        const __nv_bfloat16* qrow1 = qrow0 + 8 * a.q_sh;
+        const bool v0 = g < G, v1 = g + 8 < G;
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c0 = 16 * i + 2 * t4, c1 = 16 * i + 8 + 2 * t4;
+          qa[i][0] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0) : 0u;
+          qa[i][1] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0) : 0u;
+          qa[i][2] = v0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c1) : 0u;
+          qa[i][3] = v1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c1) : 0u;
+        }
       }
     }
     const int mi = lane >> 3;
@@ -576,8 +621,8 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int key0 = k_beg + s * STAGE_KEYS + warp * 16;
       if (key0 < k_end) {
         const int last = min(key0 + 15, k_end - 1);
-        const int Lmax = snap_levels(a, q_pos - (pos0 + last));
-        const int Lmin = snap_levels(a, q_pos - (pos0 + key0));
+        const int Lmax = decode::levels_of(lim, last);
+        const int Lmin = decode::levels_of(lim, key0);
         // rows past the item end may hold anything (the TMA box covers the
         // whole page slice): zero their V so that P = 0 rows add exactly 0
         if (last < key0 + 15) {
@@ -591,88 +636,165 @@ __global__ void __launch_bounds__(THREADS, 2)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
         }
-        float sc[2][4];
+        if constexpr (KR) {
+          // this thread's keys: key0 + g (c[0], c[1]) and key0 + g + 8 (c[2], c[3]);
+          // its heads: 2 t4 (c[0], c[2]) and 2 t4 + 1 (c[1], c[3])
+          const int key_a = key0 + g, key_b = key0 + g + 8;
+          const bool ok_a = key_a <= last, ok_b = key_b <= last;
+          const int La = decode::levels_of(lim, key_a);
+          const int Lb = decode::levels_of(lim, key_b);
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
+          const uint32_t krow = static_cast<uint32_t>(lrow * 32 + 16 * ((mi & 1) ^ ((lrow >> 2) & 1)));
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
-        const uint32_t krow = static_cast<uint32_t>(lrow * 32 + 16 * ((mi & 1) ^ ((lrow >> 2) & 1)));
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (i < Lmax) {
-            uint32_t b0, b1, b2, b3;
-            decode::ldsm_x4(kb + k_slice + i * lstride + krow, b0, b1, b2, b3);
-            if (i < Lmin) {
-              decode::mma16816(sc[0], qa[i], b0, b1);
-              decode::mma16816(sc[1], qa[i], b2, b3);
-            } else {
-              // level i is active only for the newer keys of the group
-              float tmp[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-              decode::mma16816(tmp[0], qa[i], b0, b1);
-              decode::mma16816(tmp[1], qa[i], b2, b3);
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
-                  if (key <= last && i < snap_levels(a, q_pos - (pos0 + key))) sc[nt][e] += tmp[nt][e];
+          for (int i = 0; i < 8; ++i) {
+            if (i < Lmax) {
+              // matrices: keys 0-7 / 8-15 x dims 0-7 / 8-15 of level i
+              uint32_t m0, m1, m2, m3;
+              decode::ldsm_x4(kb + k_slice + i * lstride + krow, m0, m1, m2, m3);
+              const uint32_t ak[4] = {m0, m2, m1, m3};
+              if (i < Lmin) {
+                decode::mma16816(c, ak, qb[i][0], qb[i][1]);
+              } else {
+                // level i is active only for the newer keys of the group
+                float t[4] = {0.f, 0.f, 0.f, 0.f};
+                decode::mma16816(t, ak, qb[i][0], qb[i][1]);
+                if (i < La) {
+                  c[0] += t[0];
+                  c[1] += t[1];
                 }
+                if (i < Lb) {
+                  c[2] += t[2];
+                  c[3] += t[3];
+                }
+              }
             }
           }
-        }
-        float mloc[2] = {-INFINITY, -INFINITY};
+          const float sl = a.scale_log2;
+          const float s0 = ok_a ? c[0] * sl : -INFINITY, s1 = ok_a ? c[1] * sl : -INFINITY;
+          const float s2 = ok_b ? c[2] * sl : -INFINITY, s3 = ok_b ? c[3] * sl : -INFINITY;
+          // per-head maxima over the group's 16 keys (the 8 lanes of equal t4)
+          float mh0 = fmaxf(s0, s2), mh1 = fmaxf(s1, s3);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
-            const float v = key <= last ? sc[nt][e] * a.scale_log2 : -INFINITY;
-            sc[nt][e] = v;
-            mloc[e >> 1] = fmaxf(mloc[e >> 1], v);
+          for (int off = 4; off < 32; off <<= 1) {
+            mh0 = fmaxf(mh0, __shfl_xor_sync(FULLMASK, mh0, off));
+            mh1 = fmaxf(mh1, __shfl_xor_sync(FULLMASK, mh1, off));
           }
-        float alpha[2], psum[2];
+          const float mn0 = fmaxf(m_run[0], mh0), mn1 = fmaxf(m_run[1], mh1);
+          const float al0 = (m_run[0] == -INFINITY) ? 0.f : decode::ex2f(m_run[0] - mn0);
+          const float al1 = (m_run[1] == -INFINITY) ? 0.f : decode::ex2f(m_run[1] - mn1);
+          m_run[0] = mn0;
+          m_run[1] = mn1;
+          const float p0 = decode::ex2f(s0 - mn0), p1 = decode::ex2f(s1 - mn1);
+          const float p2 = decode::ex2f(s2 - mn0), p3 = decode::ex2f(s3 - mn1);
+          l_run[0] = l_run[0] * al0 + (p0 + p2);
+          l_run[1] = l_run[1] * al1 + (p1 + p3);
+          // P^T (keys x heads) as the B operand: transpose the (key, head) blocks
+          // of keys 0-7 and 8-15
+          const uint32_t pb0 = decode::movmatrix_t(decode::pack2(p0, p1));
+          const uint32_t pb1 = decode::movmatrix_t(decode::pack2(p2, p3));
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 1));
-          mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 2));
-          const float mnew = fmaxf(m_run[r], mloc[r]);
-          alpha[r] = (m_run[r] == -INFINITY) ? 0.f : decode::ex2f(m_run[r] - mnew);
-          m_run[r] = mnew;
-          psum[r] = 0.f;
-        }
-        uint32_t pfrag[4];
+          for (int j = 0; j < 8; ++j) {
+            o[j][0] *= al0;
+            o[j][1] *= al1;
+            o[j][2] *= al0;
+            o[j][3] *= al1;
+          }
+          const int vrow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const float p0 = decode::ex2f(sc[nt][0] - m_run[0]);
-          const float p1 = decode::ex2f(sc[nt][1] - m_run[0]);
-          const float p2 = decode::ex2f(sc[nt][2] - m_run[1]);
-          const float p3 = decode::ex2f(sc[nt][3] - m_run[1]);
-          psum[0] += p0 + p1;
-          psum[1] += p2 + p3;
-          pfrag[2 * nt + 0] = decode::pack2(p0, p1);
-          pfrag[2 * nt + 1] = decode::pack2(p2, p3);
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 1);
-          psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 2);
-          l_run[r] = l_run[r] * alpha[r] + psum[r];
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          o[j][0] *= alpha[0];
-          o[j][1] *= alpha[0];
-          o[j][2] *= alpha[1];
-          o[j][3] *= alpha[1];
-        }
-        const int vrow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int dc = 2 * jj + (mi >> 1);  // 8-dim chunk 0..15
-          uint32_t b0, b1, b2, b3;
-          decode::ldsm_x4_t(vb + v_slice + (dc >> 3) * hstride + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
-                            b0, b1, b2, b3);
-          decode::mma16816(o[2 * jj], pfrag, b0, b1);
-          decode::mma16816(o[2 * jj + 1], pfrag, b2, b3);
+          for (int jj = 0; jj < 8; ++jj) {
+            const int dc = 2 * jj + (mi >> 1);  // 8-dim chunk 0..15
+            uint32_t m0, m1, m2, m3;
+            decode::ldsm_x4_t(vb + v_slice + (dc >> 3) * hstride + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
+                              m0, m1, m2, m3);
+            // V^T (dims 16jj..16jj+15 x the 16 keys) as the A operand
+            const uint32_t av[4] = {m0, m2, m1, m3};
+            decode::mma16816(o[jj], av, pb0, pb1);
+          }
+        } else {
+          float sc[2][4];
+  #pragma unroll
+          for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+          const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
+          const uint32_t krow = static_cast<uint32_t>(lrow * 32 + 16 * ((mi & 1) ^ ((lrow >> 2) & 1)));
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (i < Lmax) {
+              uint32_t b0, b1, b2, b3;
+              decode::ldsm_x4(kb + k_slice + i * lstride + krow, b0, b1, b2, b3);
+              if (i < Lmin) {
+                decode::mma16816(sc[0], qa[i], b0, b1);
+                decode::mma16816(sc[1], qa[i], b2, b3);
+              } else {
+                // level i is active only for the newer keys of the group
+                float tmp[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                decode::mma16816(tmp[0], qa[i], b0, b1);
+                decode::mma16816(tmp[1], qa[i], b2, b3);
+  #pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
+                    if (key <= last && i < decode::levels_of(lim, key)) sc[nt][e] += tmp[nt][e];
+                  }
+              }
+            }
+          }
+          float mloc[2] = {-INFINITY, -INFINITY};
+  #pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = key0 + nt * 8 + 2 * t4 + (e & 1);
+              const float v = key <= last ? sc[nt][e] * a.scale_log2 : -INFINITY;
+              sc[nt][e] = v;
+              mloc[e >> 1] = fmaxf(mloc[e >> 1], v);
+            }
+          float alpha[2], psum[2];
+  #pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 1));
+            mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(FULLMASK, mloc[r], 2));
+            const float mnew = fmaxf(m_run[r], mloc[r]);
+            alpha[r] = (m_run[r] == -INFINITY) ? 0.f : decode::ex2f(m_run[r] - mnew);
+            m_run[r] = mnew;
+            psum[r] = 0.f;
+          }
+          uint32_t pfrag[4];
+  #pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const float p0 = decode::ex2f(sc[nt][0] - m_run[0]);
+            const float p1 = decode::ex2f(sc[nt][1] - m_run[0]);
+            const float p2 = decode::ex2f(sc[nt][2] - m_run[1]);
+            const float p3 = decode::ex2f(sc[nt][3] - m_run[1]);
+            psum[0] += p0 + p1;
+            psum[1] += p2 + p3;
+            pfrag[2 * nt + 0] = decode::pack2(p0, p1);
+            pfrag[2 * nt + 1] = decode::pack2(p2, p3);
+          }
+  #pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 1);
+            psum[r] += __shfl_xor_sync(FULLMASK, psum[r], 2);
+            l_run[r] = l_run[r] * alpha[r] + psum[r];
+          }
+  #pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            o[j][0] *= alpha[0];
+            o[j][1] *= alpha[0];
+            o[j][2] *= alpha[1];
+            o[j][3] *= alpha[1];
+          }
+          const int vrow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
+  #pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int dc = 2 * jj + (mi >> 1);  // 8-dim chunk 0..15
+            uint32_t b0, b1, b2, b3;
+            decode::ldsm_x4_t(vb + v_slice + (dc >> 3) * hstride + vrow * 128 + 16 * ((dc & 7) ^ (vrow & 7)),
+                              b0, b1, b2, b3);
+            decode::mma16816(o[2 * jj], pfrag, b0, b1);
+            decode::mma16816(o[2 * jj + 1], pfrag, b2, b3);
+          }
         }
       }
       __syncwarp();
@@ -686,19 +808,43 @@ __global__ void __launch_bounds__(THREADS, 2)
   float* sm_m = sm_o + CONSUMERS * 16 * 128;        // [4][16]
   float* sm_l = sm_m + CONSUMERS * 16;
   if (warp < CONSUMERS) {
+    if constexpr (KR) {
+      // O^T fragments: dims 16j + g (+ 8) of heads 2 t4 and 2 t4 + 1; the row
+      // sums are still per thread (its two keys per stage): add the 8 key rows
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = 8 * j + 2 * t4;
-      sm_o[(warp * 16 + g) * 128 + col] = o[j][0];
-      sm_o[(warp * 16 + g) * 128 + col + 1] = o[j][1];
-      sm_o[(warp * 16 + g + 8) * 128 + col] = o[j][2];
-      sm_o[(warp * 16 + g + 8) * 128 + col + 1] = o[j][3];
-    }
-    if (t4 == 0) {
-      sm_m[warp * 16 + g] = m_run[0];
-      sm_m[warp * 16 + g + 8] = m_run[1];
-      sm_l[warp * 16 + g] = l_run[0];
-      sm_l[warp * 16 + g + 8] = l_run[1];
+      for (int off = 4; off < 32; off <<= 1) {
+        l_run[0] += __shfl_xor_sync(FULLMASK, l_run[0], off);
+        l_run[1] += __shfl_xor_sync(FULLMASK, l_run[1], off);
+      }
+      float* r0 = sm_o + (warp * 16 + 2 * t4) * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        r0[16 * j + g] = o[j][0];
+        r0[128 + 16 * j + g] = o[j][1];
+        r0[16 * j + g + 8] = o[j][2];
+        r0[128 + 16 * j + g + 8] = o[j][3];
+      }
+      if (g == 0) {
+        sm_m[warp * 16 + 2 * t4] = m_run[0];
+        sm_m[warp * 16 + 2 * t4 + 1] = m_run[1];
+        sm_l[warp * 16 + 2 * t4] = l_run[0];
+        sm_l[warp * 16 + 2 * t4 + 1] = l_run[1];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = 8 * j + 2 * t4;
+        sm_o[(warp * 16 + g) * 128 + col] = o[j][0];
+        sm_o[(warp * 16 + g) * 128 + col + 1] = o[j][1];
+        sm_o[(warp * 16 + g + 8) * 128 + col] = o[j][2];
+        sm_o[(warp * 16 + g + 8) * 128 + col + 1] = o[j][3];
+      }
+      if (t4 == 0) {
+        sm_m[warp * 16 + g] = m_run[0];
+        sm_m[warp * 16 + g + 8] = m_run[1];
+        sm_l[warp * 16 + g] = l_run[0];
+        sm_l[warp * 16 + g + 8] = l_run[1];
+      }
     }
   }
   __syncthreads();
@@ -1000,10 +1146,12 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
       ta.d = a;
       ta.rows = static_cast<int>(rows);
       ta.err = p->error_flag;
-      if (cudaFuncSetAttribute(decode_tma::decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               decode_tma::SMEM_BYTES) != cudaSuccess)
+      // groups of at most 8 query heads: keys as the MMA rows
+      auto kern = a.G <= 8 ? decode_tma::decode_tma_kernel<true> : decode_tma::decode_tma_kernel<false>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_tma::SMEM_BYTES) !=
+          cudaSuccess)
         return ATF_ERR_CUDA;
-      decode_tma::decode_tma_kernel<<<grid, decode_tma::THREADS, decode_tma::SMEM_BYTES, st>>>(tk, tv, ta);
+      kern<<<grid, decode_tma::THREADS, decode_tma::SMEM_BYTES, st>>>(tk, tv, ta);
     } else {
       if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                decode::SMEM_BYTES) != cudaSuccess)
