@@ -179,19 +179,38 @@ struct Args {
   long long cs_stride;
 };
 
-__device__ __forceinline__ int levels_for(const Args& a, int row0, int j) {
-  if (!a.window) return 8;
-  long long z = a.q_offset + row0 - (static_cast<long long>(j) * BN + BN - 1);
-  if (z < 0) z = 0;
+// The window of one query tile (rows row0..row0+127) as key-tile limits, set
+// once per CTA and held in registers: key tile j reads level i when
+// j >= lim[i]. The tile's smallest distance is z_min(j) = max(0, q_offset + row0
+// - (128 j + 127)), and level i is read when z_min(j) <= zhi[i] (level 0
+// always: zhi[0] covers every distance), i.e. from
+// j = ceil((q_offset + row0 - 127 - zhi[i]) / 128) on.
+__device__ __forceinline__ void window_limits(const Args& a, int row0, int (&lim)[ATF_MAX_LEVELS]) {
+  const long long base = a.q_offset + row0 - (BN - 1);
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) {
+    const long long x = base - a.zhi[i];
+    long long j = (!a.window || i == 0 || x <= 0) ? 0 : (x + BN - 1) / BN;
+    lim[i] = static_cast<int>(j > 0x7fffffffLL ? 0x7fffffffLL : j);
+  }
+}
+// levels of key tile j: the L (1..8) in-window 16-dim levels of the pair
+__device__ __forceinline__ int levels_for(const int (&lim)[ATF_MAX_LEVELS], int j) {
   int L = 0;
 #pragma unroll
-  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += (static_cast<long long>(a.zhi[i]) >= z) ? 1 : 0;
-  return L < 1 ? 1 : L;
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) L += j >= lim[i] ? 1 : 0;
+  return L;
 }
-
-__device__ __forceinline__ bool needs_mask(const Args& a, int row0, int j) {
-  const long long n_last = static_cast<long long>(j) * BN + BN - 1;
-  return (a.causal && n_last > a.q_offset + row0) || n_last >= a.Sk;
+// first key tile that needs per-element masks: a key past the query row
+// (causal) or past the end of the keys
+__device__ __forceinline__ int first_masked_tile(const Args& a, int row0) {
+  long long jm = a.Sk / BN;  // 128 j + 127 >= Sk from j = ceil((Sk - 127) / 128) = floor(Sk / 128)
+  if (a.causal) {
+    const long long x = a.q_offset + row0 - (BN - 1);  // 128 j > x for a masked tile
+    const long long jc = x < 0 ? 0 : x / BN + 1;
+    if (jc < jm) jm = jc;
+  }
+  return static_cast<int>(jm > 0x7fffffffLL ? 0x7fffffffLL : jm);
 }
 
 // Column of the first element of half `hh` of level `i` along head_dim.
@@ -251,6 +270,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
   const int nk_max = nk[0] > nk[1] ? nk[0] : nk[1];
+  int lim[NQ][ATF_MAX_LEVELS];
+#pragma unroll
+  for (int t = 0; t < NQ; ++t) window_limits(a, row0[t], lim[t]);
 
   if (threadIdx.x == 0) {
     *s_abort = (a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0) ? 1 : 0;
@@ -320,7 +342,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int t = 0; t < NQ; ++t)
         if (j < nk[t]) {
-          const int lt = levels_for(a, row0[t], j);
+          const int lt = levels_for(lim[t], j);
           L = lt > L ? lt : L;
         }
       const uint32_t kdst = sb + OFF_K + ks * KSTAGE_BYTES;
@@ -368,7 +390,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool sorted = a.layout == ATF_LAYOUT_SORTED_PAIR;
     const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
     auto issue_S = [&](int t, int j) {
-      const int L = levels_for(a, row0[t], j);
+      const int L = levels_for(lim[t], j);
       const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
       const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
       if (sorted)
@@ -443,6 +465,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tO = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_off;
     const int my_row0 = t ? row0[1] : row0[0];
     const int my_nk = t ? nk[1] : nk[0];
+    const int j_mask = first_masked_tile(a, my_row0);
     const int qrow = my_row0 + r;
     const long long qpos = a.q_offset + qrow;
     const float sl2 = a.scale_log2;
@@ -481,7 +504,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
       }
-      if (needs_mask(a, my_row0, j)) {
+      if (j >= j_mask) {
         const long long n0 = static_cast<long long>(j) * BN;
 #pragma unroll
         for (int c = 0; c < BN; ++c) {
