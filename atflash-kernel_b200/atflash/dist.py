@@ -16,6 +16,7 @@ give the result.
 The reference has no multi-GPU code (it is batch-1, single GPU); this module is
 the build's sharding of the same computation.
 """
+import functools
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -26,6 +27,12 @@ TILE = 128
 
 
 def zigzag_bounds(seqlen: int, world: int, align: int = TILE, zhi: Optional[Sequence[int]] = None) -> List[int]:
+    """2*world+1 query block boundaries (see _zigzag_bounds); cached per shape."""
+    return list(_zigzag_bounds(int(seqlen), int(world), int(align), None if zhi is None else tuple(int(x) for x in zhi)))
+
+
+@functools.lru_cache(maxsize=64)
+def _zigzag_bounds(seqlen: int, world: int, align: int, zhi: Optional[Tuple[int, ...]]) -> Tuple[int, ...]:
     """2*world+1 block boundaries, interior ones on multiples of `align`.
 
     Without a window table the blocks have equal rows: under a causal mask the
@@ -44,7 +51,7 @@ def zigzag_bounds(seqlen: int, world: int, align: int = TILE, zhi: Optional[Sequ
         equal.append(min(max(x, equal[-1]), seqlen))
     equal.append(seqlen)
     if zhi is None or world == 1:
-        return equal
+        return tuple(equal)
     cum = _cumulative_tile_work(seqlen, zhi, align)  # cum[t]: work of rows [0, t * align)
     nt = len(cum) - 1
     half = int(round(nt / 2))
@@ -61,7 +68,7 @@ def zigzag_bounds(seqlen: int, world: int, align: int = TILE, zhi: Optional[Sequ
     tail.append(half)
     b = [min(x * align, seqlen) for x in b[:-1] + tail[::-1]]
     # the cuts sit on whole tiles, so keep whichever split is closer to even
-    return b if _max_pair_work(b, cum, world, align) < _max_pair_work(equal, cum, world, align) else equal
+    return tuple(b if _max_pair_work(b, cum, world, align) < _max_pair_work(equal, cum, world, align) else equal)
 
 
 def _max_pair_work(b, cum, world, align):
@@ -71,16 +78,19 @@ def _max_pair_work(b, cum, world, align):
 
 
 def _cumulative_tile_work(seqlen: int, zhi: Sequence[int], tile: int = TILE, head_dim: int = 128):
-    """Windowed work of the rows [0, t * tile) for every t (causal prefill, one head)."""
+    """Windowed work of the rows [0, t * tile) for every t (causal prefill, one head).
+
+    Query tile t meets key tiles n = 0..t; the pair's smallest distance
+    z = max(0, (t - n - 1) * tile + 1) depends on d = t - n only, so the work of
+    query tile t is the prefix sum over d <= t of 16 L(d) + head_dim."""
     levels = np.asarray(list(zhi), dtype=np.int64)
     nt = (seqlen + tile - 1) // tile
+    d = np.arange(nt, dtype=np.int64)
+    z = np.maximum(0, (d - 1) * tile + 1)
+    L = np.maximum(1, (levels[None, :] >= z[:, None]).sum(axis=1))
+    per_tile = np.cumsum((16 * L + head_dim).astype(np.float64))  # work of query tile t
     work = np.zeros(nt + 1, dtype=np.float64)
-    n0 = np.arange(nt, dtype=np.int64) * tile
-    for t in range(nt):
-        q0 = t * tile
-        z = np.maximum(0, q0 - (n0[:t + 1] + tile - 1))
-        L = np.maximum(1, (levels[None, :] >= z[:, None]).sum(axis=1))
-        work[t + 1] = work[t] + float((16 * L + head_dim).sum())
+    work[1:] = np.cumsum(per_tile)
     return work
 
 
