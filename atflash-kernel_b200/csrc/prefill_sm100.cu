@@ -6,12 +6,13 @@
 //   warp 8       TMA producer. Q once (8 levels x 2 halves per tile); per key
 //                tile only the in-window K levels (L = D_eff/16 of the nearer
 //                query tile) and the two 64-dim V boxes.
-//   warp 9       MMA issuer and TMEM owner (512 columns). For key tile j:
-//                O_0 += P_0(j) V_j, S_0(j+1) = Q_0 K_{j+1}^T, then the same for
-//                Q1, so each query tile's softmax overlaps the other tile's MMAs.
-//                S_t is computed over L(t, j) K-steps of 16 dims; P_t (bf16) is
-//                written back into the first 64 columns of S_t and read by the
-//                O += P V MMA straight from TMEM.
+//   warp 9       MMA issuer and TMEM owner (512 columns). S_t is computed
+//                over L(t, j) K-steps of 16 dims. P_t (bf16) goes into columns
+//                64..127 of the OTHER tile's S (free once that tile has read its
+//                scores into registers) and is read by O_t += P_t V from TMEM. So
+//                S_t(j+1) does not wait for P_t(j): per key tile j the warp issues
+//                O_0 += P_0(j) V_j, S_1(j+1), O_1 += P_1(j) V_j, S_0(j+2), and a
+//                softmax warp finds its next scores ready when it finishes a step.
 //   warps 0-3/4-7  softmax for Q0 / Q1: one query row per thread, online
 //                softmax in the log2 domain, lazy O rescale, epilogue.
 //
@@ -42,7 +43,7 @@
 //   V  2 stages x 2 boxes (dims 0-63, 64-127) x 128 keys x 128 B, 128B swizzle;
 //      the PV B operand is MN-major: LBO (next 64 dims) = 16 KB, SBO (next 8
 //      keys) = 1 KB.
-// TMEM columns: S_t at 128t, O_t at 256 + 128t.
+// TMEM columns: S_t at 128t, O_t at 256 + 128t; P_t at 128(1-t) + 64.
 #include <math.h>
 
 #include "atf_internal.h"
@@ -148,7 +149,8 @@ enum {
   B_PFULL = B_SFULL + NQ,     // [t]
   B_ODONE = B_PFULL + NQ,     // [t], one phase per O += P V
   B_OFINAL = B_ODONE + NQ,    // [t], single phase: the tile's last O += P V done
-  B_FINAL = B_OFINAL + NQ,
+  B_LOADED = B_OFINAL + NQ,   // [t], phase j: tile t's softmax has read S_t(j) into registers
+  B_FINAL = B_LOADED + NQ,
   NUM_BARS
 };
 constexpr uint32_t OFF_ABORT = OFF_BAR + 8 * NUM_BARS;
@@ -291,6 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar(B_PFULL + t), 128);
       mbar_init(bar(B_ODONE + t), 1);
       mbar_init(bar(B_OFINAL + t), 1);
+      mbar_init(bar(B_LOADED + t), 128);
     }
     mbar_init(bar(B_FINAL), 1);
     fence_mbar_init();
@@ -389,65 +392,87 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint64_t kdesc32 = make_sdesc(sb + OFF_K, 16, 256, kLayoutSw32);
     const bool sorted = a.layout == ATF_LAYOUT_SORTED_PAIR;
     const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
+    const int nk0 = nk[0], nk1 = nk[1];
+    // S_t(j) into tile t's S columns
     auto issue_S = [&](int t, int j) {
       const int L = levels_for(lim[t], j);
       const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
       const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
-      if (sorted)
-        qk_group_asm(d_tmem, qd, kdesc32 + (((j % KST) * KSTAGE_BYTES) >> 4), IDESC_QK, L, bar(B_SFULL + t));
-      else
-        qk_group_asm(d_tmem, qd, kdesc0 + (((j % KST) * KSTAGE_BYTES) >> 4), IDESC_QK, L, bar(B_SFULL + t));
+      const uint64_t kd = (sorted ? kdesc32 : kdesc0) + (((j % KST) * KSTAGE_BYTES) >> 4);
+      qk_group_asm(d_tmem, qd, kd, IDESC_QK, L, bar(B_SFULL + t));
     };
+    // O_t += P_t(j) V_j; P_t sits in columns 64..127 of the other tile's S
     auto issue_PV = [&](int t, int j) {
       const uint32_t o_tmem = tm + 256u + static_cast<uint32_t>(t * 128);
-      const uint32_t p_tmem = tm + static_cast<uint32_t>(t * 128);
+      const uint32_t p_tmem = tm + static_cast<uint32_t>((1 - t) * 128 + 64);
       const uint64_t vd = vdesc0 + (((j % VST) * VSTAGE_BYTES) >> 4);
       pv_group_asm(o_tmem, p_tmem, vd, IDESC_PV, j > 0 ? 1u : 0u, bar(B_ODONE + t));
     };
+    // K tiles are waited for in order, once each
+    int k_waited = -1;
+    auto kwait = [&](int j) -> bool {
+      while (k_waited < j) {
+        ++k_waited;
+        if (!__all_sync(FULL, mbar_wait(bar(B_KFULL + k_waited % KST), (k_waited / KST) & 1, ab,
+                                        kDevErrTimeout)))
+          return false;
+        tc_fence_after();
+      }
+      return true;
+    };
+    auto wait_loaded = [&](int t, int j) -> bool {
+      const bool w = __all_sync(FULL, mbar_wait(bar(B_LOADED + t), j & 1, ab, kDevErrTimeout));
+      tc_fence_after();
+      return w;
+    };
+    // A K stage is released after the last S that reads it: S_1(j) when tile 1
+    // has key tile j, else S_0(j).
     bool ok = __all_sync(FULL, mbar_wait(bar(B_Q), 0, ab, kDevErrTimeout));
     tc_fence_after();
-    if (ok && nk_max > 0) {
-      ok = __all_sync(FULL, mbar_wait(bar(B_KFULL + 0), 0, ab, kDevErrTimeout));
-      tc_fence_after();
-      if (ok) {
-#pragma unroll
-        for (int t = 0; t < NQ; ++t)
-          if (nk[t] > 0) issue_S(t, 0);
-        tc_commit_elect(bar(B_KEMPTY + 0));
-      }
+    if (ok && nk_max > 0 && (ok = kwait(0))) {
+      if (nk0 > 0) issue_S(0, 0);
+      if (nk1 > 0) issue_S(1, 0);
+      tc_commit_elect(bar(B_KEMPTY + 0));
+    }
+    // S_0(1) once tile 0 has read S_0(0)
+    if (ok && nk0 > 1 && (ok = kwait(1) && wait_loaded(0, 0))) {
+      issue_S(0, 1);
+      if (1 >= nk1) tc_commit_elect(bar(B_KEMPTY + 1 % KST));
     }
     for (int j = 0; ok && j < nk_max; ++j) {
       const int vs = j % VST;
       ok = __all_sync(FULL, mbar_wait(bar(B_VFULL + vs), (j / VST) & 1, ab, kDevErrTimeout));
       if (!ok) break;
       tc_fence_after();
-      bool kwaited = false;
-#pragma unroll
-      for (int t = 0; t < NQ; ++t) {
+      if (j < nk0) {
+        ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + 0), j & 1, ab, kDevErrTimeout));
         if (!ok) break;
-        if (j < nk[t]) {
-          ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + t), j & 1, ab, kDevErrTimeout));
-          if (!ok) break;
-          tc_fence_after();
-          issue_PV(t, j);
-          if (j + 1 == nk[t]) tc_commit_elect(bar(B_OFINAL + t));
-        }
-        if (j + 1 < nk[t]) {
-          if (!kwaited) {
-            const int ks = (j + 1) % KST;
-            ok = __all_sync(FULL,
-                            mbar_wait(bar(B_KFULL + ks), ((j + 1) / KST) & 1, ab, kDevErrTimeout));
-            if (!ok) break;
-            tc_fence_after();
-            kwaited = true;
-          }
-          // S_t(j+1) overwrites the TMEM columns P_t(j) occupies; the O += P V
-          // above was issued first and tcgen05.mma ops of one thread run in order.
-          issue_S(t, j + 1);
-        }
+        tc_fence_after();
+        issue_PV(0, j);
+        if (j + 1 == nk0) tc_commit_elect(bar(B_OFINAL + 0));
       }
-      if (!ok) break;
-      if (kwaited) tc_commit_elect(bar(B_KEMPTY + (j + 1) % KST));
+      // S_1(j+1) overwrites the columns P_0(j) occupies (O_0 += P_0(j) V_j was
+      // issued first; tcgen05.mma ops of one thread run in order) and needs
+      // tile 1 to have read S_1(j)
+      if (j + 1 < nk1) {
+        if (!(ok = kwait(j + 1) && wait_loaded(1, j))) break;
+        issue_S(1, j + 1);
+        tc_commit_elect(bar(B_KEMPTY + (j + 1) % KST));
+      }
+      if (j < nk1) {
+        ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + 1), j & 1, ab, kDevErrTimeout));
+        if (!ok) break;
+        tc_fence_after();
+        issue_PV(1, j);
+        if (j + 1 == nk1) tc_commit_elect(bar(B_OFINAL + 1));
+      }
+      // S_0(j+2): after O_1 += P_1(j) V_j (P_1(j) sits in S_0's columns) and
+      // tile 0's read of S_0(j+1)
+      if (j + 2 < nk0) {
+        if (!(ok = kwait(j + 2) && wait_loaded(0, j + 1))) break;
+        issue_S(0, j + 2);
+        if (j + 2 >= nk1) tc_commit_elect(bar(B_KEMPTY + (j + 2) % KST));
+      }
       tc_commit_elect(bar(B_VEMPTY + vs));
     }
     // Every MMA issued by this CTA completes before TMEM is released.
@@ -462,6 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + static_cast<uint32_t>(t * 128) + lane_off;
+    const uint32_t tP = tmem + static_cast<uint32_t>((1 - t) * 128 + 64) + lane_off;
     const uint32_t tO = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_off;
     const int my_row0 = t ? row0[1] : row0[0];
     const int my_nk = t ? nk[1] : nk[0];
@@ -504,6 +530,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
       }
+      // S_t's columns are free now: the MMA warp may compute S_t(j+1) into
+      // them, and the other tile may store its P there
+      tc_fence_before();
+      mbar_arrive(bar(B_LOADED + t));
       if (j >= j_mask) {
         const long long n0 = static_cast<long long>(j) * BN;
 #pragma unroll
@@ -557,7 +587,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float2 ls = __fadd2_rn(ls0, ls1);
         l += ls.x + ls.y;
       }
-      tmem_st64(tS, pk);
+      // P_t(j) goes into columns 64..127 of the other tile's S once the scores
+      // there have been read: S_1(j) for tile 0, S_0(j+1) for tile 1 (whose
+      // computation followed O_1 += P_1(j-1) V, the last reader of those
+      // columns). Past the other tile's last key tile, wait for its last read
+      // and for this tile's previous O += P V instead.
+      {
+        const int other_nk = t ? nk[0] : nk[1];
+        const int want = j + t;  // tile 0: S_1(j); tile 1: S_0(j + 1)
+        bool w = true;
+        if (want < other_nk) {
+          w = mbar_wait(bar(B_LOADED + (t ^ 1)), want & 1, ab, kDevErrTimeout);
+        } else {
+          if (other_nk > 0) w = mbar_wait(bar(B_LOADED + (t ^ 1)), (other_nk - 1) & 1, ab, kDevErrTimeout);
+          if (w && j > 0) w = mbar_wait(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout);
+        }
+        ok = __all_sync(FULL, w);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      tmem_st64(tP, pk);
       if (__any_sync(FULL, need)) {
         // O holds the sum up to tile j-1 once PV(t, j-1) has completed (S_t(j) was
         // issued after it, so at most that one is in flight); PV(t, j) is not
