@@ -162,6 +162,28 @@ def test_prefill_qk_path_identity_values(cuda_device):
     assert err < 5e-3, err
 
 
+@pytest.mark.parametrize("sq,sk", [(384, 640), (200, 333), (640, 640)])
+def test_prefill_noncausal_multi_tile(cuda_device, sq, sk):
+    """Non-causal, window off, both query tiles of a CTA over several key tiles
+    (equal key-tile counts, so every step's P goes to the other tile's S
+    columns), ragged tails: against a plain torch fp32 attention."""
+    atflash = _atf()
+    hq, hkv = 4, 2
+    g = torch.Generator().manual_seed(sq * 1000 + sk)
+    q = torch.randn((1, sq, hq, 128), generator=g).to(torch.bfloat16)
+    k = torch.randn((1, sk, hkv, 128), generator=g).to(torch.bfloat16)
+    v = torch.randn((1, sk, hkv, 128), generator=g).to(torch.bfloat16)
+    out = atflash.flash_attn_func(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), causal=False)
+    torch.cuda.synchronize()
+    assert atflash.check_device_errors() == 0
+    kk = k.float().repeat_interleave(hq // hkv, dim=2)
+    vv = v.float().repeat_interleave(hq // hkv, dim=2)
+    s = torch.einsum("bqhd,bkhd->bhqk", q.float(), kk) / math.sqrt(128)
+    ref = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(s, -1), vv)
+    mx, mean = err_stats(out.float().cpu().numpy(), ref.numpy())
+    assert mx <= MAX_ABS_TOL and mean <= MEAN_ABS_TOL, (mx, mean)
+
+
 @pytest.mark.parametrize("layout", ["rotate_half"])
 def test_prefill_rotate_half_layout(cuda_device, layout):
     """HF rotate_half q/k read in place (level halves are dims [56-8i,64-8i) and
