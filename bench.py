@@ -1037,6 +1037,9 @@ def main():
         h2d = kv_h2d + sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         d2h = sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        # consecutive query chunks alternate between two compute streams, so a
+        # chunk's launch fills the SMs its predecessor's tail leaves idle
+        comp = [torch.cuda.Stream(device), torch.cuda.Stream(device)]
         comm = torch.cuda.Stream(device) if shard_kv else None
         ev_up = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
         ev_kv = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
@@ -1088,16 +1091,22 @@ def main():
                         ev_q[n].record(up)
             if used[b]:
                 main.wait_event(ev_out_free[b])
+            for cs in comp:
+                cs.wait_stream(main)
             for n, (c0, c1) in enumerate(chunks):
-                main.wait_event(ev_q[n])
+                cs = comp[n % 2]
+                cs.wait_event(ev_q[n])
                 if shard_kv:  # every key range below c1 has been gathered
-                    main.wait_event(ev_kv[next(c for c in range(KV_CHUNKS) if kv_bounds[c + 1] >= c1)])
-                atflash.flash_attn_func(qd[:, c0:c1], kd[:, :c1], vd[:, :c1], causal=True, window_table=wt2,
-                                        q_offset=c0, out=outd[:, c0:c1])
-                ev_o[n].record(main)
+                    cs.wait_event(ev_kv[next(c for c in range(KV_CHUNKS) if kv_bounds[c + 1] >= c1)])
+                with torch.cuda.stream(cs):
+                    atflash.flash_attn_func(qd[:, c0:c1], kd[:, :c1], vd[:, :c1], causal=True, window_table=wt2,
+                                            q_offset=c0, out=outd[:, c0:c1])
+                ev_o[n].record(cs)
                 down.wait_event(ev_o[n])
                 with torch.cuda.stream(down):
                     outh[:, c0:c1].copy_(outd[:, c0:c1], non_blocking=True)
+            for cs in comp:
+                main.wait_stream(cs)
             ev_in_free[b].record(main)
             ev_out_free[b].record(down)
             used[b] = True
@@ -1116,7 +1125,8 @@ def main():
                            f"ranges and an NCCL all-gather over NVLink completes each range on every rank; a copy "
                            f"stream sends the rank's q rows, " if shard_kv else
                            f"a copy stream sends each chunk's new k/v rows and its q rows, ") +
-                           f"and each chunk's output goes down on another while later chunks compute; two "
+                           f"and each chunk's output goes down on another while later chunks compute (consecutive chunks "
+                           f"alternate between two compute streams, so one's launch fills the other's tail); two "
                            f"device buffer sets alternate by step, so a step's copies overlap the previous "
                            f"step's compute; the last step's copies complete inside the timed region"}
         del sets
