@@ -41,7 +41,7 @@ class AtfPrefillParams(ctypes.Structure):
                 ("q_offset", _i64), ("softmax_scale", _f32), ("causal", ctypes.c_int),
                 ("qk_layout", ctypes.c_int), ("window", ctypes.c_int), ("zhi", _i32 * 8),
                 ("error_flag", _vp), ("q_cos", _vp), ("q_sin", _vp), ("q_cs_stride_pos", _i64),
-                ("q_n_pos", _i64)]
+                ("q_n_pos", _i64), ("num_row_ranges", _i32), ("row_begin", _i64 * 2), ("row_end", _i64 * 2)]
 
 
 class AtfDecodePlanParams(ctypes.Structure):

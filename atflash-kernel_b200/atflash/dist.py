@@ -129,9 +129,12 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=
     """This rank's zig-zag share of a causal prefill over the full q/k/v.
 
     Returns [(start, end, out_block)] for the rank's two blocks, or with
-    gather=True the full (B, S, Hq, D) output assembled by an all-gather."""
-    if prefill_fn is None:
-        from .prefill import prefill_fwd as prefill_fn
+    gather=True the full (B, S, Hq, D) output assembled by an all-gather.
+
+    Both blocks go out as one kernel launch over the full q/k/v (the kernel's
+    row ranges), so they share one launch tail; the blocks are views of one
+    (B, S, Hq, D) buffer whose other rows are left unwritten. A custom
+    `prefill_fn` (a host-side model of the kernel, say) is called per block."""
     r0, w0 = _rank_world(group)
     rank = r0 if rank is None else rank
     world = w0 if world is None else world
@@ -139,8 +142,20 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=
     if k.shape[1] != S:
         raise ValueError("sharded prefill expects seqlen_q == seqlen_k")
     zhi = getattr(window_table, "zhi16", None) if causal else None
+    blocks = zigzag_blocks(S, world, rank, zhi=zhi)
+    if prefill_fn is None:
+        from .prefill import prefill_fwd
+        live = [(s, e) for (s, e) in blocks if e > s]
+        full = q.new_empty(q.shape)
+        if live:
+            prefill_fwd(q, k, v, causal=causal, softmax_scale=softmax_scale, window_table=window_table,
+                        qk_layout=qk_layout, q_offset=0, out=full, row_ranges=live)
+        outs = [(s, e, full[:, s:e]) for (s, e) in blocks]
+        if not gather:
+            return outs
+        return gather_zigzag(outs, S, world, group, zhi=zhi)
     outs = []
-    for (s, e) in zigzag_blocks(S, world, rank, zhi=zhi):
+    for (s, e) in blocks:
         if e <= s:
             outs.append((s, e, q.new_empty((q.shape[0], 0, q.shape[2], q.shape[3]))))
             continue

@@ -57,12 +57,16 @@ def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bo
                 softmax_scale: Optional[float] = None, window_table: WindowSpec = None,
                 qk_layout: str = "sorted_pair", q_offset: Optional[int] = None,
                 out: Optional[torch.Tensor] = None, return_lse: bool = False,
-                q_rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+                q_rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                row_ranges: Optional[Sequence[Tuple[int, int]]] = None):
     """Run the tcgen05 windowed prefill kernel. q (B, Sq, Hq, 128), k/v (B, Sk, Hkv, 128).
 
     q_rope: optional fp32 (cos, sin) tables (n_pos, >= 64): q is then pre-RoPE in
     rotate_half order and the kernel rotates each query row at position
-    q_offset + row as it loads it (k must be post-RoPE, sorted pairs)."""
+    q_offset + row as it loads it (k must be post-RoPE, sorted pairs).
+    row_ranges: up to two sorted, disjoint [begin, end) ranges of query rows,
+    begins on multiples of 128: only those rows of out are computed, in one
+    launch (the rows are bit-identical to a run over all rows)."""
     _check_qkv(q, k, v)
     dev = _runtime.require_cuda(q, k, v)
     B, Sq, Hq, D = q.shape
@@ -98,6 +102,16 @@ def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bo
         for i, z in enumerate(zhi):
             p.zhi[i] = z
     p.error_flag = _runtime.error_flag(dev).data_ptr()
+    if row_ranges is not None:
+        rr = [(int(b), int(e)) for (b, e) in row_ranges]
+        if not 1 <= len(rr) <= 2:
+            raise ValueError("row_ranges holds one or two ranges")
+        for i, (b, e) in enumerate(rr):
+            if b < 0 or e <= b or e > Sq or b % 128 or (i and b < rr[i - 1][1]):
+                raise ValueError("row ranges must be sorted, disjoint, non-empty, inside the rows and "
+                                 "begin on multiples of 128")
+            p.row_begin[i], p.row_end[i] = b, e
+        p.num_row_ranges = len(rr)
     if q_rope is not None:
         cos, sin = q_rope
         if qk_layout != "sorted_pair":

@@ -164,6 +164,10 @@ constexpr uint32_t FULL = 0xffffffffu;
 
 struct Args {
   int B, Sq, Sk, Hq, G, n_qblk;
+  // query row ranges: range r covers rows [r_lo[r], r_hi[r]) in r_nblk[r] blocks
+  // of BM * NQ rows; n_qblk is their sum
+  int nrange;
+  int r_lo[2], r_hi[2], r_nblk[2];
   long long q_offset;
   float scale_log2;
   int causal, layout, window;
@@ -255,15 +259,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int per_group = a.n_qblk * a.G;
   const int grp = static_cast<int>(blockIdx.x) / per_group;
   const int rem = static_cast<int>(blockIdx.x) % per_group;
-  const int qblk = a.n_qblk - 1 - rem / a.G;
+  // blocks of the later row range first, each range's blocks latest rows first
+  const int qidx = a.n_qblk - 1 - rem / a.G;
+  const int rng = (a.nrange > 1 && qidx >= a.r_nblk[0]) ? 1 : 0;
+  const int row_base = a.r_lo[rng] + (qidx - (rng ? a.r_nblk[0] : 0)) * (BM * NQ);
+  const int row_end = rng ? a.r_hi[1] : a.r_hi[0];
   const int bi = grp / Hkv;
   const int hk = grp % Hkv;
   const int h = hk * a.G + rem % a.G;
   int row0[NQ], nk[NQ];
 #pragma unroll
   for (int t = 0; t < NQ; ++t) {
-    row0[t] = qblk * (BM * NQ) + t * BM;
-    if (row0[t] >= a.Sq) {
+    row0[t] = row_base + t * BM;
+    if (row0[t] >= row_end) {
       nk[t] = 0;
     } else {
       long long kend = a.causal ? a.q_offset + row0[t] + BM : a.Sk;
@@ -500,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // rounded to bf16, into the sorted-pair Q slabs (level i = HF pairs
       // 8(7-i)..8(7-i)+7); rows past the end are zero
       uint8_t* qt = sp + OFF_Q + t * QTILE_BYTES + r * 16;
-      const bool valid = my_nk > 0 && qrow < a.Sq;
+      const bool valid = my_nk > 0 && qrow < row_end;
       const __nv_bfloat16* xr = a.q + static_cast<long long>(bi) * a.q_sb + static_cast<long long>(qrow) * a.q_ss +
                                 static_cast<long long>(h) * a.q_sh;
       const float* cr = a.qcos + qpos * a.cs_stride;
@@ -631,7 +639,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        const bool store = qrow < a.Sq;
+        const bool store = qrow < row_end;
         __nv_bfloat16* orow = a.out + static_cast<long long>(bi) * a.o_sb +
                               static_cast<long long>(qrow) * a.o_ss +
                               static_cast<long long>(h) * a.o_sh;
@@ -707,6 +715,12 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     // zhi[0] must cover the largest distance in the problem (D_eff >= 16 always).
     if (static_cast<int64_t>(p->zhi[0]) < p->q_offset + p->seqlen_q - 1) return ATF_ERR_INVALID_ARG;
   }
+  if (p->num_row_ranges < 0 || p->num_row_ranges > 2) return ATF_ERR_INVALID_ARG;
+  for (int r = 0; r < p->num_row_ranges; ++r) {
+    const int64_t lo = p->row_begin[r], hi = p->row_end[r];
+    if (lo < 0 || hi <= lo || hi > p->seqlen_q || (lo % BM) != 0) return ATF_ERR_INVALID_ARG;
+    if (r > 0 && lo < p->row_end[r - 1]) return ATF_ERR_INVALID_ARG;
+  }
   int dev = 0;
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
@@ -758,7 +772,23 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
   a.Sk = static_cast<int>(p->seqlen_k);
   a.Hq = static_cast<int>(p->num_heads_q);
   a.G = static_cast<int>(p->num_heads_q / p->num_heads_kv);
-  a.n_qblk = static_cast<int>((p->seqlen_q + BM * NQ - 1) / (BM * NQ));
+  if (p->num_row_ranges == 0) {
+    a.nrange = 1;
+    a.r_lo[0] = 0;
+    a.r_hi[0] = static_cast<int>(p->seqlen_q);
+  } else {
+    a.nrange = p->num_row_ranges;
+    for (int r = 0; r < a.nrange; ++r) {
+      a.r_lo[r] = static_cast<int>(p->row_begin[r]);
+      a.r_hi[r] = static_cast<int>(p->row_end[r]);
+    }
+  }
+  a.n_qblk = 0;
+  for (int r = 0; r < 2; ++r) {
+    a.r_nblk[r] = r < a.nrange ? (a.r_hi[r] - a.r_lo[r] + BM * NQ - 1) / (BM * NQ) : 0;
+    if (r >= a.nrange) a.r_lo[r] = a.r_hi[r] = 0;
+    a.n_qblk += a.r_nblk[r];
+  }
   a.q_offset = p->q_offset;
   a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
   a.causal = p->causal ? 1 : 0;

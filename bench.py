@@ -889,12 +889,11 @@ def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
     out = torch.empty_like(q)
     wt = atflash.WindowTable(D, THETA, K_RET)
     blocks = atflash.dist.zigzag_blocks(N, world, rank, zhi=wt.zhi16) if world > 1 else [(0, N)]
+    live = [b for b in blocks if b[1] > b[0]]
 
     def fn(i):
-        for (s0, e0) in blocks:
-            if e0 > s0:
-                atflash.prefill_fwd(q[:, s0:e0], k[:, :e0], v[:, :e0], causal=True, window_table=wt,
-                                    q_offset=s0, out=out[:, s0:e0])
+        # this rank's zig-zag blocks in one launch (the kernel's row ranges)
+        atflash.prefill_fwd(q, k, v, causal=True, window_table=wt, q_offset=0, out=out, row_ranges=live)
     ms, _ = timed(fn, steps, warmup, world)
     work = WT.prefill_work(HQ, N, N, wt.zhi16)
     mine = sum(WT.prefill_work(HQ, e0 - s0, e0, wt.zhi16, q_offset=s0)["flops"] for (s0, e0) in blocks if e0 > s0)
@@ -962,15 +961,14 @@ def main():
     wt2 = atflash.WindowTable(D, THETA, K_RET)
     blocks = atflash.dist.zigzag_blocks(N_CTX, world, rank, zhi=wt2.zhi16) if world > 1 else [(0, N_CTX)]
     out = torch.empty((1, N_CTX, HQ, D), dtype=torch.bfloat16, device=device)
-    launches_per_step = len([b for b in blocks if b[1] > b[0]])
+    live = [b for b in blocks if b[1] > b[0]]
+    launches_per_step = 1
 
     def step(wt):
         def fn(i):
+            # this rank's zig-zag blocks (the whole sequence at N=1) in one launch
             q, k, v = inputs[i % len(inputs)]
-            for (s, e) in blocks:
-                if e > s:
-                    atflash.prefill_fwd(q[:, s:e], k[:, :e], v[:, :e], causal=True, window_table=wt,
-                                        q_offset=s, out=out[:, s:e])
+            atflash.prefill_fwd(q, k, v, causal=True, window_table=wt, q_offset=0, out=out, row_ranges=live)
         return fn
 
     sampler = ClockSampler(local)

@@ -121,6 +121,15 @@ typedef struct {
   const float* q_sin;
   int64_t q_cs_stride_pos; /* elements between the tables' rows */
   int64_t q_n_pos;         /* rows in the tables; q_offset + seqlen_q <= q_n_pos */
+  /* Row ranges (optional): with num_row_ranges = 1 or 2, only the query rows
+   * [row_begin[i], row_end[i]) are computed, in one launch; the other rows of
+   * out (and lse) are neither read nor written. A rank of a zig-zag sharded
+   * prefill passes its two blocks here. Ranges are sorted, disjoint, inside
+   * [0, seqlen_q), and begin on multiples of 128 (the query tile, so the window's
+   * tile quantisation is the single run's). 0: every row. */
+  int32_t num_row_ranges;
+  int64_t row_begin[2];
+  int64_t row_end[2];
 } AtfPrefillParams;
 
 /* Windowed causal prefill on the tcgen05/TMEM kernel. Tiles are 128 queries x

@@ -162,6 +162,26 @@ def test_prefill_qk_path_identity_values(cuda_device):
     assert err < 5e-3, err
 
 
+def test_prefill_row_ranges_one_launch(cuda_device):
+    """Two row ranges in one launch (a zig-zag rank's blocks): their rows equal the
+    same rows of the full run bit for bit, and no other row of out is written."""
+    atflash = _atf()
+    q, k, v, _ = make_bhsd(6, 2, 1280, 128, 1e4, 31)
+    q, k, v = (_bshd(t, cuda_device) for t in (q, k, v))
+    wt = atflash.WindowTable(128, 1e4, 2.0)
+    full = atflash.prefill_fwd(q, k, v, causal=True, window_table=wt)
+    out = torch.full_like(q, 7.0)
+    ranges = [(128, 384), (896, 1200)]
+    atflash.prefill_fwd(q, k, v, causal=True, window_table=wt, q_offset=0, out=out, row_ranges=ranges)
+    torch.cuda.synchronize()
+    assert atflash.check_device_errors() == 0
+    keep = torch.zeros(1280, dtype=torch.bool)
+    for (b, e) in ranges:
+        keep[b:e] = True
+        assert torch.equal(out[:, b:e].view(torch.int16), full[:, b:e].view(torch.int16)), (b, e)
+    assert bool((out[:, ~keep.to(cuda_device)] == 7.0).all())
+
+
 @pytest.mark.parametrize("sq,sk", [(384, 640), (200, 333), (640, 640)])
 def test_prefill_noncausal_multi_tile(cuda_device, sq, sk):
     """Non-causal, window off, both query tiles of a CTA over several key tiles

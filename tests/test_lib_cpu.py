@@ -83,6 +83,15 @@ def test_invalid_arguments_rejected_without_gpu():
     for i, z in enumerate((100, 50, 60, 10, 0, 0, 0, 0)):
         p.zhi[i] = z
     assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -1  # levels must not widen
+    p.window = _ffi.ATF_WINDOW_OFF
+    p.seqlen_q = p.seqlen_k = 1024
+    for ranges in (((64, 256),), ((0, 256), (128, 512)), ((256, 128),), ((0, 1100),), ((0, 128),) * 3):
+        p.num_row_ranges = len(ranges)
+        for i, (b, e) in enumerate(ranges[:2]):
+            p.row_begin[i], p.row_end[i] = b, e
+        # unaligned begin, overlapping, empty, past the rows, more than two ranges
+        assert lib.atf_prefill_fwd(ctypes.byref(p), None) == -1, ranges
+    p.num_row_ranges = 0
     d = _ffi.AtfDecodeParams()
     d.q = d.k_cache = d.v_cache = d.indptr = d.indices = d.last_page_len = 16
     d.items = d.item_indptr = d.partial_o = d.partial_lse = d.out = 16
