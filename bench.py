@@ -1036,8 +1036,10 @@ def main():
         d2h = sum((c1 - c0) * HQ * D * 2 for (c0, c1) in chunks)
         up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
         # consecutive query chunks alternate between two compute streams, so a
-        # chunk's launch fills the SMs its predecessor's tail leaves idle
-        comp = [torch.cuda.Stream(device), torch.cuda.Stream(device)]
+        # chunk's launch fills the SMs its predecessor's tail leaves idle; with
+        # the K/V all-gathers running beside them (several ranks) one stream, so
+        # that the NCCL kernels are not starved of SMs
+        comp = [torch.cuda.Stream(device) for _ in range(1 if shard_kv else 2)]
         comm = torch.cuda.Stream(device) if shard_kv else None
         ev_up = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
         ev_kv = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
@@ -1092,7 +1094,7 @@ def main():
             for cs in comp:
                 cs.wait_stream(main)
             for n, (c0, c1) in enumerate(chunks):
-                cs = comp[n % 2]
+                cs = comp[n % len(comp)]
                 cs.wait_event(ev_q[n])
                 if shard_kv:  # every key range below c1 has been gathered
                     cs.wait_event(ev_kv[next(c for c in range(KV_CHUNKS) if kv_bounds[c + 1] >= c1)])
@@ -1123,8 +1125,9 @@ def main():
                            f"ranges and an NCCL all-gather over NVLink completes each range on every rank; a copy "
                            f"stream sends the rank's q rows, " if shard_kv else
                            f"a copy stream sends each chunk's new k/v rows and its q rows, ") +
-                           f"and each chunk's output goes down on another while later chunks compute (consecutive chunks "
-                           f"alternate between two compute streams, so one's launch fills the other's tail); two "
+                           f"and each chunk's output goes down on another while later chunks compute" +
+                           (f"; " if shard_kv else f" (consecutive chunks alternate between two compute streams, so "
+                                                     f"one's launch fills the other's tail); ") + f"two "
                            f"device buffer sets alternate by step, so a step's copies overlap the previous "
                            f"step's compute; the last step's copies complete inside the timed region"}
         del sets
