@@ -1040,7 +1040,10 @@ def main():
         # the K/V all-gathers running beside them (several ranks) one stream, so
         # that the NCCL kernels are not starved of SMs
         comp = [torch.cuda.Stream(device) for _ in range(1 if shard_kv else 2)]
-        comm = torch.cuda.Stream(device) if shard_kv else None
+        # the K/V all-gathers at high priority: their NCCL kernels get SMs as soon
+        # as a prefill CTA frees one, so that no rank's gather waits behind a
+        # whole prefill chunk (a collective completes only when every rank's has run)
+        comm = torch.cuda.Stream(device, priority=-1) if shard_kv else None
         ev_up = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
         ev_kv = [torch.cuda.Event() for _ in range(KV_CHUNKS)]
         ev_q = [torch.cuda.Event() for _ in chunks]
