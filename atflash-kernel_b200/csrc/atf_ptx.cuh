@@ -88,6 +88,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const A
   return mbar_wait_slow(bar, parity, a, code);
 }
 
+// The same wait with its slow path inlined, for kernels that split registers
+// between warpgroups (setmaxnreg): a function called from regions with
+// different register budgets cannot be allocated.
+__device__ __forceinline__ bool mbar_wait_inl(uint32_t bar, uint32_t parity, const AbortCtl& a,
+                                              int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (aborted(a)) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *a.smem_flag = 1;
+        if (a.gflag != nullptr) atomicCAS(a.gflag, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

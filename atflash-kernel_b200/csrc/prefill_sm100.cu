@@ -119,7 +119,23 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 
 constexpr int BM = 128, BN = 128, HD = 128, NQ = 2, KST = 2, VST = 2;
-constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 10, THREADS = NUM_WARPS * 32;
+// Warps 10 and 11 have no role: they complete the third warpgroup so that the
+// register split below (setmaxnreg acts on whole warpgroups) can take
+// registers from the producer / MMA group and give them to the softmax groups.
+constexpr int WARP_LOAD = 8, WARP_MMA = 9, NUM_WARPS = 12, THREADS = NUM_WARPS * 32;
+// Registers per thread after the split. The block launches with THREADS x the
+// compiled count (168 under __launch_bounds__(THREADS, 1)); the host refuses to
+// launch unless 128 x REG_SMALL + 256 x REG_SOFTMAX fits in that.
+constexpr int REG_SMALL = 80, REG_SOFTMAX = 208;
+constexpr long long REG_SPLIT_TOTAL = 128LL * REG_SMALL + 256LL * REG_SOFTMAX;
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 constexpr uint32_t QHALF_BYTES = BM * 16;             // 2 KB
 constexpr uint32_t QSLAB_BYTES = 2 * QHALF_BYTES;     // 4 KB
 constexpr uint32_t QTILE_BYTES = 8 * QSLAB_BYTES;     // 32 KB
@@ -322,346 +338,351 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *s_tmem;
   const AbortCtl ab{s_abort, a.err};
   const bool start_ok = (*s_abort == 0);
-
-  if (start_ok && warp == WARP_LOAD) {
-    // ---------------------------------------------------------------- producer
-    // All 32 lanes run this loop with warp-uniform values; one elected lane
-    // issues each TMA / expect_tx.
-    int issued_k = 0, issued_v = 0;
-    bool ok = true;
-    if (!a.qrot) {
-      uint32_t qbytes = 0;
+  if (warp >= 8) {
+    reg_dealloc<REG_SMALL>();
+    if (start_ok && warp == WARP_LOAD) {
+      // ---------------------------------------------------------------- producer
+      // All 32 lanes run this loop with warp-uniform values; one elected lane
+      // issues each TMA / expect_tx.
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      if (!a.qrot) {
+        uint32_t qbytes = 0;
 #pragma unroll
-      for (int t = 0; t < NQ; ++t) qbytes += nk[t] > 0 ? QTILE_BYTES : 0u;
-      mbar_arrive_expect_tx_elect(bar(B_Q), qbytes);
+        for (int t = 0; t < NQ; ++t) qbytes += nk[t] > 0 ? QTILE_BYTES : 0u;
+        mbar_arrive_expect_tx_elect(bar(B_Q), qbytes);
 #pragma unroll
-      for (int t = 0; t < NQ; ++t) {
-        if (nk[t] == 0) continue;
+        for (int t = 0; t < NQ; ++t) {
+          if (nk[t] == 0) continue;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+          for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh)
-            tma_load_4d_elect(sb + OFF_Q + t * QTILE_BYTES + i * QSLAB_BYTES + hh * QHALF_BYTES, &tmQ,
-                              bar(B_Q), level_col(a.layout, i, hh), row0[t], h, bi);
-      }
-    }
-    for (int j = 0; j < nk_max; ++j) {
-      const int ks = j % KST, vs = j % VST;
-      ok = __all_sync(FULL, mbar_wait(bar(B_KEMPTY + ks), ((j / KST) & 1) ^ 1, ab, kDevErrTimeout));
-      if (!ok) break;
-      int L = 0;
-#pragma unroll
-      for (int t = 0; t < NQ; ++t)
-        if (j < nk[t]) {
-          const int lt = levels_for(lim[t], j);
-          L = lt > L ? lt : L;
-        }
-      const uint32_t kdst = sb + OFF_K + ks * KSTAGE_BYTES;
-      if (a.layout == ATF_LAYOUT_SORTED_PAIR) {
-        // one 5-d box: the L in-window levels (dims 0..16L-1), one 4 KB slab each
-        mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
-        if (elect_one_lane()) tma_load_5d(kdst, &tmKL.lv[L - 1], bar(B_KFULL + ks), 0, j * BN, 0, hk, bi);
-        __syncwarp();
-      } else {
-        // rotate_half: a level is two 8-dim chunks 64 dims apart, one box each
-        mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
-        for (int i = 0; i < L; ++i) {
-          tma_load_4d_elect(kdst + i * KSLAB_BYTES, &tmK, bar(B_KFULL + ks), level_col(a.layout, i, 0),
-                            j * BN, hk, bi);
-          tma_load_4d_elect(kdst + i * KSLAB_BYTES + KHALF_BYTES, &tmK, bar(B_KFULL + ks),
-                            level_col(a.layout, i, 1), j * BN, hk, bi);
+            for (int hh = 0; hh < 2; ++hh)
+              tma_load_4d_elect(sb + OFF_Q + t * QTILE_BYTES + i * QSLAB_BYTES + hh * QHALF_BYTES, &tmQ,
+                                bar(B_Q), level_col(a.layout, i, hh), row0[t], h, bi);
         }
       }
-      issued_k = j + 1;
-      ok = __all_sync(FULL, mbar_wait(bar(B_VEMPTY + vs), ((j / VST) & 1) ^ 1, ab, kDevErrTimeout));
-      if (!ok) break;
-      mbar_arrive_expect_tx_elect(bar(B_VFULL + vs), VSTAGE_BYTES);
-      tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES, &tmV, bar(B_VFULL + vs), 0, j * BN, hk, bi);
-      tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES + VBOX_BYTES, &tmV, bar(B_VFULL + vs), 64,
-                        j * BN, hk, bi);
-      issued_v = j + 1;
-    }
-    // Drain: every copy this warp issued must land before shared memory is
-    // released (no-op on the normal path, where the MMA warp consumed them).
-    drain_wait(bar(B_Q), 0);
-    for (int j = issued_k - KST; j < issued_k; ++j)
-      if (j >= 0) drain_wait(bar(B_KFULL + j % KST), (j / KST) & 1);
-    for (int j = issued_v - VST; j < issued_v; ++j)
-      if (j >= 0) drain_wait(bar(B_VFULL + j % VST), (j / VST) & 1);
-    __syncwarp();
-  } else if (start_ok && warp == WARP_MMA) {
-    // ---------------------------------------------------------------- MMA issuer
-    // Descriptors are built once and advanced by adding (byte offset >> 4) to
-    // the start-address field (all offsets stay inside the 14-bit field).
-    const uint32_t tm = __shfl_sync(FULL, tmem, 0);
-    const uint64_t qdesc0 = make_sdesc(sb + OFF_Q, QHALF_BYTES, 128, kLayoutNone);
-    const uint64_t kdesc0 = make_sdesc(sb + OFF_K, KHALF_BYTES, 128, kLayoutNone);
-    // sorted-pair K level slabs: 128 keys x 32 B, 32-byte swizzle (SBO = 8 rows)
-    const uint64_t kdesc32 = make_sdesc(sb + OFF_K, 16, 256, kLayoutSw32);
-    const bool sorted = a.layout == ATF_LAYOUT_SORTED_PAIR;
-    const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
-    const int nk0 = nk[0], nk1 = nk[1];
-    // S_t(j) into tile t's S columns
-    auto issue_S = [&](int t, int j) {
-      const int L = levels_for(lim[t], j);
-      const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
-      const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
-      const uint64_t kd = (sorted ? kdesc32 : kdesc0) + (((j % KST) * KSTAGE_BYTES) >> 4);
-      qk_group_asm(d_tmem, qd, kd, IDESC_QK, L, bar(B_SFULL + t));
-    };
-    // O_t += P_t(j) V_j; P_t sits in columns 64..127 of the other tile's S
-    auto issue_PV = [&](int t, int j) {
-      const uint32_t o_tmem = tm + 256u + static_cast<uint32_t>(t * 128);
-      const uint32_t p_tmem = tm + static_cast<uint32_t>((1 - t) * 128 + 64);
-      const uint64_t vd = vdesc0 + (((j % VST) * VSTAGE_BYTES) >> 4);
-      pv_group_asm(o_tmem, p_tmem, vd, IDESC_PV, j > 0 ? 1u : 0u, bar(B_ODONE + t));
-    };
-    // K tiles are waited for in order, once each
-    int k_waited = -1;
-    auto kwait = [&](int j) -> bool {
-      while (k_waited < j) {
-        ++k_waited;
-        if (!__all_sync(FULL, mbar_wait(bar(B_KFULL + k_waited % KST), (k_waited / KST) & 1, ab,
-                                        kDevErrTimeout)))
-          return false;
-        tc_fence_after();
-      }
-      return true;
-    };
-    auto wait_loaded = [&](int t, int j) -> bool {
-      const bool w = __all_sync(FULL, mbar_wait(bar(B_LOADED + t), j & 1, ab, kDevErrTimeout));
-      tc_fence_after();
-      return w;
-    };
-    // A K stage is released after the last S that reads it: S_1(j) when tile 1
-    // has key tile j, else S_0(j).
-    bool ok = __all_sync(FULL, mbar_wait(bar(B_Q), 0, ab, kDevErrTimeout));
-    tc_fence_after();
-    if (ok && nk_max > 0 && (ok = kwait(0))) {
-      if (nk0 > 0) issue_S(0, 0);
-      if (nk1 > 0) issue_S(1, 0);
-      tc_commit_elect(bar(B_KEMPTY + 0));
-    }
-    // S_0(1) once tile 0 has read S_0(0)
-    if (ok && nk0 > 1 && (ok = kwait(1) && wait_loaded(0, 0))) {
-      issue_S(0, 1);
-      if (1 >= nk1) tc_commit_elect(bar(B_KEMPTY + 1 % KST));
-    }
-    for (int j = 0; ok && j < nk_max; ++j) {
-      const int vs = j % VST;
-      ok = __all_sync(FULL, mbar_wait(bar(B_VFULL + vs), (j / VST) & 1, ab, kDevErrTimeout));
-      if (!ok) break;
-      tc_fence_after();
-      if (j < nk0) {
-        ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + 0), j & 1, ab, kDevErrTimeout));
+      for (int j = 0; j < nk_max; ++j) {
+        const int ks = j % KST, vs = j % VST;
+        ok = __all_sync(FULL, mbar_wait_inl(bar(B_KEMPTY + ks), ((j / KST) & 1) ^ 1, ab, kDevErrTimeout));
         if (!ok) break;
-        tc_fence_after();
-        issue_PV(0, j);
-        if (j + 1 == nk0) tc_commit_elect(bar(B_OFINAL + 0));
-      }
-      // S_1(j+1) overwrites the columns P_0(j) occupies (O_0 += P_0(j) V_j was
-      // issued first; tcgen05.mma ops of one thread run in order) and needs
-      // tile 1 to have read S_1(j)
-      if (j + 1 < nk1) {
-        if (!(ok = kwait(j + 1) && wait_loaded(1, j))) break;
-        issue_S(1, j + 1);
-        tc_commit_elect(bar(B_KEMPTY + (j + 1) % KST));
-      }
-      if (j < nk1) {
-        ok = __all_sync(FULL, mbar_wait(bar(B_PFULL + 1), j & 1, ab, kDevErrTimeout));
-        if (!ok) break;
-        tc_fence_after();
-        issue_PV(1, j);
-        if (j + 1 == nk1) tc_commit_elect(bar(B_OFINAL + 1));
-      }
-      // S_0(j+2): after O_1 += P_1(j) V_j (P_1(j) sits in S_0's columns) and
-      // tile 0's read of S_0(j+1)
-      if (j + 2 < nk0) {
-        if (!(ok = kwait(j + 2) && wait_loaded(0, j + 1))) break;
-        issue_S(0, j + 2);
-        if (j + 2 >= nk1) tc_commit_elect(bar(B_KEMPTY + (j + 2) % KST));
-      }
-      tc_commit_elect(bar(B_VEMPTY + vs));
-    }
-    // Every MMA issued by this CTA completes before TMEM is released.
-    tc_commit_elect(bar(B_FINAL));
-    __syncwarp();
-    drain_wait(bar(B_FINAL), 0);
-    __syncwarp();
-  } else if (start_ok && warp < 8) {
-    // ---------------------------------------------------------------- softmax
-    const int t = warp >> 2;
-    const int wq = warp & 3;
-    const int r = wq * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + static_cast<uint32_t>(t * 128) + lane_off;
-    const uint32_t tP = tmem + static_cast<uint32_t>((1 - t) * 128 + 64) + lane_off;
-    const uint32_t tO = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_off;
-    const int my_row0 = t ? row0[1] : row0[0];
-    const int my_nk = t ? nk[1] : nk[0];
-    const int j_mask = first_masked_tile(a, my_row0);
-    const int qrow = my_row0 + r;
-    const long long qpos = a.q_offset + qrow;
-    const float sl2 = a.scale_log2;
-    if (a.qrot) {
-      // RoPE at load: this thread's query row, rotated in fp32 at its position,
-      // rounded to bf16, into the sorted-pair Q slabs (level i = HF pairs
-      // 8(7-i)..8(7-i)+7); rows past the end are zero
-      uint8_t* qt = sp + OFF_Q + t * QTILE_BYTES + r * 16;
-      const bool valid = my_nk > 0 && qrow < row_end;
-      const __nv_bfloat16* xr = a.q + static_cast<long long>(bi) * a.q_sb + static_cast<long long>(qrow) * a.q_ss +
-                                static_cast<long long>(h) * a.q_sh;
-      const float* cr = a.qcos + qpos * a.cs_stride;
-      const float* sr = a.qsin + qpos * a.cs_stride;
+        int L = 0;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (valid) ropemath::rotate_chunk_sorted_words(xr, cr, sr, c, w);
-        uint8_t* slab = qt + (7 - c) * QSLAB_BYTES;
-        *reinterpret_cast<uint4*>(slab) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(slab + QHALF_BYTES) = make_uint4(w[4], w[5], w[6], w[7]);
-      }
-      // the MMAs read Q through the async proxy
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(bar(B_Q));
-    }
-    float m2 = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < my_nk; ++j) {
-      ok = __all_sync(FULL, mbar_wait(bar(B_SFULL + t), j & 1, ab, kDevErrTimeout));
-      if (!ok) break;
-      tc_fence_after();
-      float s[BN];
-      {
-        uint32_t rr[BN];
-        tmem_ld128(tS, rr);
-#pragma unroll
-        for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
-      }
-      // S_t's columns are free now: the MMA warp may compute S_t(j+1) into
-      // them, and the other tile may store its P there
-      tc_fence_before();
-      mbar_arrive(bar(B_LOADED + t));
-      if (j >= j_mask) {
-        const long long n0 = static_cast<long long>(j) * BN;
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const long long key = n0 + c;
-          if ((a.causal && key > qpos) || key >= a.Sk) s[c] = -INFINITY;
-        }
-      }
-      // three-input max: 64 instructions for the 128 scores, 4 chains
-      float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
-      float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
-#pragma unroll
-      for (int c = 12; c < BN - 8; c += 8) {
-        mx0 = fmax3(mx0, s[c], s[c + 1]);
-        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
-        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
-        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
-      }
-      mx0 = fmax3(mx0, s[BN - 4], s[BN - 3]);
-      mx1 = fmax3(mx1, s[BN - 2], s[BN - 1]);
-      const float mnew = fmaxf(m2, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
-      // Lazy rescale: the running max only moves when it grows by more than
-      // 8 (log2 units), so P <= 2^8 stays exact enough in bf16 and O is
-      // rescaled rarely. The O update itself happens after P is stored.
-      float alpha = 1.0f;
-      bool need = false;
-      if (j == 0) {
-        m2 = mnew;
-      } else {
-        need = mnew > m2 + 8.0f;
-        if (need) {
-          alpha = ex2_approx(m2 - mnew);
-          l *= alpha;
-          m2 = mnew;
-        }
-      }
-      const float msub = (m2 == -INFINITY) ? 0.f : m2;
-      // exponentials, the row sum and the bf16 packing of P, two columns at a
-      // time with packed f32x2 arithmetic (half the FMA / add instructions)
-      uint32_t pk[BN / 2];
-      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
-      const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
-#pragma unroll
-      for (int c = 0; c < BN / 2; ++c) {
-        const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sl2x2, negm);
-        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        if (c & 1) ls1 = __fadd2_rn(ls1, p); else ls0 = __fadd2_rn(ls0, p);
-        pk[c] = pack_bf16x2(p.x, p.y);
-      }
-      {
-        const float2 ls = __fadd2_rn(ls0, ls1);
-        l += ls.x + ls.y;
-      }
-      // P_t(j) goes into columns 64..127 of the other tile's S once the scores
-      // there have been read: S_1(j) for tile 0, S_0(j+1) for tile 1 (whose
-      // computation followed O_1 += P_1(j-1) V, the last reader of those
-      // columns). Past the other tile's last key tile, wait for its last read
-      // and for this tile's previous O += P V instead.
-      {
-        const int other_nk = t ? nk[0] : nk[1];
-        const int want = j + t;  // tile 0: S_1(j); tile 1: S_0(j + 1)
-        bool w = true;
-        if (want < other_nk) {
-          w = mbar_wait(bar(B_LOADED + (t ^ 1)), want & 1, ab, kDevErrTimeout);
+        for (int t = 0; t < NQ; ++t)
+          if (j < nk[t]) {
+            const int lt = levels_for(lim[t], j);
+            L = lt > L ? lt : L;
+          }
+        const uint32_t kdst = sb + OFF_K + ks * KSTAGE_BYTES;
+        if (a.layout == ATF_LAYOUT_SORTED_PAIR) {
+          // one 5-d box: the L in-window levels (dims 0..16L-1), one 4 KB slab each
+          mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
+          if (elect_one_lane()) tma_load_5d(kdst, &tmKL.lv[L - 1], bar(B_KFULL + ks), 0, j * BN, 0, hk, bi);
+          __syncwarp();
         } else {
-          if (other_nk > 0) w = mbar_wait(bar(B_LOADED + (t ^ 1)), (other_nk - 1) & 1, ab, kDevErrTimeout);
-          if (w && j > 0) w = mbar_wait(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout);
-        }
-        ok = __all_sync(FULL, w);
-        if (!ok) break;
-        tc_fence_after();
-      }
-      tmem_st64(tP, pk);
-      if (__any_sync(FULL, need)) {
-        // O holds the sum up to tile j-1 once PV(t, j-1) has completed (S_t(j) was
-        // issued after it, so at most that one is in flight); PV(t, j) is not
-        // issued before this warpgroup arrives on PFULL below.
-        ok = __all_sync(FULL, mbar_wait(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int c4 = 0; c4 < HD / 32; ++c4) {
-          uint32_t rr[32];
-          tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-          tmem_st32(tO + static_cast<uint32_t>(32 * c4), rr);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bar(B_PFULL + t));
-    }
-    if (ok && my_nk > 0) {
-      ok = __all_sync(FULL, mbar_wait(bar(B_OFINAL + t), 0, ab, kDevErrTimeout));
-      if (ok) {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.0f / l : 0.f;
-        const bool store = qrow < row_end;
-        __nv_bfloat16* orow = a.out + static_cast<long long>(bi) * a.o_sb +
-                              static_cast<long long>(qrow) * a.o_ss +
-                              static_cast<long long>(h) * a.o_sh;
-#pragma unroll
-        for (int c4 = 0; c4 < HD / 32; ++c4) {
-          uint32_t rr[32];
-          tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            pk[e] = pack_bf16x2(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
-          if (store) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c4);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4)
-              dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+          // rotate_half: a level is two 8-dim chunks 64 dims apart, one box each
+          mbar_arrive_expect_tx_elect(bar(B_KFULL + ks), static_cast<uint32_t>(L) * KSLAB_BYTES);
+          for (int i = 0; i < L; ++i) {
+            tma_load_4d_elect(kdst + i * KSLAB_BYTES, &tmK, bar(B_KFULL + ks), level_col(a.layout, i, 0),
+                              j * BN, hk, bi);
+            tma_load_4d_elect(kdst + i * KSLAB_BYTES + KHALF_BYTES, &tmK, bar(B_KFULL + ks),
+                              level_col(a.layout, i, 1), j * BN, hk, bi);
           }
         }
-        if (a.lse != nullptr && store)
-          a.lse[(static_cast<long long>(bi) * a.Hq + h) * a.Sq + qrow] =
-              (m2 + log2f(l)) * 0.69314718055994531f;
+        issued_k = j + 1;
+        ok = __all_sync(FULL, mbar_wait_inl(bar(B_VEMPTY + vs), ((j / VST) & 1) ^ 1, ab, kDevErrTimeout));
+        if (!ok) break;
+        mbar_arrive_expect_tx_elect(bar(B_VFULL + vs), VSTAGE_BYTES);
+        tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES, &tmV, bar(B_VFULL + vs), 0, j * BN, hk, bi);
+        tma_load_4d_elect(sb + OFF_V + vs * VSTAGE_BYTES + VBOX_BYTES, &tmV, bar(B_VFULL + vs), 64,
+                          j * BN, hk, bi);
+        issued_v = j + 1;
       }
+      // Drain: every copy this warp issued must land before shared memory is
+      // released (no-op on the normal path, where the MMA warp consumed them).
+      drain_wait(bar(B_Q), 0);
+      for (int j = issued_k - KST; j < issued_k; ++j)
+        if (j >= 0) drain_wait(bar(B_KFULL + j % KST), (j / KST) & 1);
+      for (int j = issued_v - VST; j < issued_v; ++j)
+        if (j >= 0) drain_wait(bar(B_VFULL + j % VST), (j / VST) & 1);
+      __syncwarp();
+    } else if (start_ok && warp == WARP_MMA) {
+      // ---------------------------------------------------------------- MMA issuer
+      // Descriptors are built once and advanced by adding (byte offset >> 4) to
+      // the start-address field (all offsets stay inside the 14-bit field).
+      const uint32_t tm = __shfl_sync(FULL, tmem, 0);
+      const uint64_t qdesc0 = make_sdesc(sb + OFF_Q, QHALF_BYTES, 128, kLayoutNone);
+      const uint64_t kdesc0 = make_sdesc(sb + OFF_K, KHALF_BYTES, 128, kLayoutNone);
+      // sorted-pair K level slabs: 128 keys x 32 B, 32-byte swizzle (SBO = 8 rows)
+      const uint64_t kdesc32 = make_sdesc(sb + OFF_K, 16, 256, kLayoutSw32);
+      const bool sorted = a.layout == ATF_LAYOUT_SORTED_PAIR;
+      const uint64_t vdesc0 = make_sdesc(sb + OFF_V, VBOX_BYTES, 1024, kLayoutSw128);
+      const int nk0 = nk[0], nk1 = nk[1];
+      // S_t(j) into tile t's S columns
+      auto issue_S = [&](int t, int j) {
+        const int L = levels_for(lim[t], j);
+        const uint32_t d_tmem = tm + static_cast<uint32_t>(t * 128);
+        const uint64_t qd = qdesc0 + ((t * QTILE_BYTES) >> 4);
+        const uint64_t kd = (sorted ? kdesc32 : kdesc0) + (((j % KST) * KSTAGE_BYTES) >> 4);
+        qk_group_asm(d_tmem, qd, kd, IDESC_QK, L, bar(B_SFULL + t));
+      };
+      // O_t += P_t(j) V_j; P_t sits in columns 64..127 of the other tile's S
+      auto issue_PV = [&](int t, int j) {
+        const uint32_t o_tmem = tm + 256u + static_cast<uint32_t>(t * 128);
+        const uint32_t p_tmem = tm + static_cast<uint32_t>((1 - t) * 128 + 64);
+        const uint64_t vd = vdesc0 + (((j % VST) * VSTAGE_BYTES) >> 4);
+        pv_group_asm(o_tmem, p_tmem, vd, IDESC_PV, j > 0 ? 1u : 0u, bar(B_ODONE + t));
+      };
+      // K tiles are waited for in order, once each
+      int k_waited = -1;
+      auto kwait = [&](int j) -> bool {
+        while (k_waited < j) {
+          ++k_waited;
+          if (!__all_sync(FULL, mbar_wait_inl(bar(B_KFULL + k_waited % KST), (k_waited / KST) & 1, ab,
+                                          kDevErrTimeout)))
+            return false;
+          tc_fence_after();
+        }
+        return true;
+      };
+      auto wait_loaded = [&](int t, int j) -> bool {
+        const bool w = __all_sync(FULL, mbar_wait_inl(bar(B_LOADED + t), j & 1, ab, kDevErrTimeout));
+        tc_fence_after();
+        return w;
+      };
+      // A K stage is released after the last S that reads it: S_1(j) when tile 1
+      // has key tile j, else S_0(j).
+      bool ok = __all_sync(FULL, mbar_wait_inl(bar(B_Q), 0, ab, kDevErrTimeout));
+      tc_fence_after();
+      if (ok && nk_max > 0 && (ok = kwait(0))) {
+        if (nk0 > 0) issue_S(0, 0);
+        if (nk1 > 0) issue_S(1, 0);
+        tc_commit_elect(bar(B_KEMPTY + 0));
+      }
+      // S_0(1) once tile 0 has read S_0(0)
+      if (ok && nk0 > 1 && (ok = kwait(1) && wait_loaded(0, 0))) {
+        issue_S(0, 1);
+        if (1 >= nk1) tc_commit_elect(bar(B_KEMPTY + 1 % KST));
+      }
+      for (int j = 0; ok && j < nk_max; ++j) {
+        const int vs = j % VST;
+        ok = __all_sync(FULL, mbar_wait_inl(bar(B_VFULL + vs), (j / VST) & 1, ab, kDevErrTimeout));
+        if (!ok) break;
+        tc_fence_after();
+        if (j < nk0) {
+          ok = __all_sync(FULL, mbar_wait_inl(bar(B_PFULL + 0), j & 1, ab, kDevErrTimeout));
+          if (!ok) break;
+          tc_fence_after();
+          issue_PV(0, j);
+          if (j + 1 == nk0) tc_commit_elect(bar(B_OFINAL + 0));
+        }
+        // S_1(j+1) overwrites the columns P_0(j) occupies (O_0 += P_0(j) V_j was
+        // issued first; tcgen05.mma ops of one thread run in order) and needs
+        // tile 1 to have read S_1(j)
+        if (j + 1 < nk1) {
+          if (!(ok = kwait(j + 1) && wait_loaded(1, j))) break;
+          issue_S(1, j + 1);
+          tc_commit_elect(bar(B_KEMPTY + (j + 1) % KST));
+        }
+        if (j < nk1) {
+          ok = __all_sync(FULL, mbar_wait_inl(bar(B_PFULL + 1), j & 1, ab, kDevErrTimeout));
+          if (!ok) break;
+          tc_fence_after();
+          issue_PV(1, j);
+          if (j + 1 == nk1) tc_commit_elect(bar(B_OFINAL + 1));
+        }
+        // S_0(j+2): after O_1 += P_1(j) V_j (P_1(j) sits in S_0's columns) and
+        // tile 0's read of S_0(j+1)
+        if (j + 2 < nk0) {
+          if (!(ok = kwait(j + 2) && wait_loaded(0, j + 1))) break;
+          issue_S(0, j + 2);
+          if (j + 2 >= nk1) tc_commit_elect(bar(B_KEMPTY + (j + 2) % KST));
+        }
+        tc_commit_elect(bar(B_VEMPTY + vs));
+      }
+      // Every MMA issued by this CTA completes before TMEM is released.
+      tc_commit_elect(bar(B_FINAL));
+      __syncwarp();
+      drain_wait(bar(B_FINAL), 0);
+      __syncwarp();
+    }
+  } else {
+    reg_alloc<REG_SOFTMAX>();
+    if (start_ok) {
+        // ---------------------------------------------------------------- softmax
+        const int t = warp >> 2;
+        const int wq = warp & 3;
+        const int r = wq * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t tS = tmem + static_cast<uint32_t>(t * 128) + lane_off;
+        const uint32_t tP = tmem + static_cast<uint32_t>((1 - t) * 128 + 64) + lane_off;
+        const uint32_t tO = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_off;
+        const int my_row0 = t ? row0[1] : row0[0];
+        const int my_nk = t ? nk[1] : nk[0];
+        const int j_mask = first_masked_tile(a, my_row0);
+        const int qrow = my_row0 + r;
+        const long long qpos = a.q_offset + qrow;
+        const float sl2 = a.scale_log2;
+        if (a.qrot) {
+          // RoPE at load: this thread's query row, rotated in fp32 at its position,
+          // rounded to bf16, into the sorted-pair Q slabs (level i = HF pairs
+          // 8(7-i)..8(7-i)+7); rows past the end are zero
+          uint8_t* qt = sp + OFF_Q + t * QTILE_BYTES + r * 16;
+          const bool valid = my_nk > 0 && qrow < row_end;
+          const __nv_bfloat16* xr = a.q + static_cast<long long>(bi) * a.q_sb + static_cast<long long>(qrow) * a.q_ss +
+                                    static_cast<long long>(h) * a.q_sh;
+          const float* cr = a.qcos + qpos * a.cs_stride;
+          const float* sr = a.qsin + qpos * a.cs_stride;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (valid) ropemath::rotate_chunk_sorted_words(xr, cr, sr, c, w);
+            uint8_t* slab = qt + (7 - c) * QSLAB_BYTES;
+            *reinterpret_cast<uint4*>(slab) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(slab + QHALF_BYTES) = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+          // the MMAs read Q through the async proxy
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(bar(B_Q));
+        }
+        float m2 = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < my_nk; ++j) {
+          ok = __all_sync(FULL, mbar_wait_inl(bar(B_SFULL + t), j & 1, ab, kDevErrTimeout));
+          if (!ok) break;
+          tc_fence_after();
+          float s[BN];
+          {
+            uint32_t rr[BN];
+            tmem_ld128(tS, rr);
+#pragma unroll
+            for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
+          }
+          // S_t's columns are free now: the MMA warp may compute S_t(j+1) into
+          // them, and the other tile may store its P there
+          tc_fence_before();
+          mbar_arrive(bar(B_LOADED + t));
+          if (j >= j_mask) {
+            const long long n0 = static_cast<long long>(j) * BN;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+              const long long key = n0 + c;
+              if ((a.causal && key > qpos) || key >= a.Sk) s[c] = -INFINITY;
+            }
+          }
+          // three-input max: 64 instructions for the 128 scores, 4 chains
+          float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+          float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
+#pragma unroll
+          for (int c = 12; c < BN - 8; c += 8) {
+            mx0 = fmax3(mx0, s[c], s[c + 1]);
+            mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+            mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+            mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
+          }
+          mx0 = fmax3(mx0, s[BN - 4], s[BN - 3]);
+          mx1 = fmax3(mx1, s[BN - 2], s[BN - 1]);
+          const float mnew = fmaxf(m2, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+          // Lazy rescale: the running max only moves when it grows by more than
+          // 8 (log2 units), so P <= 2^8 stays exact enough in bf16 and O is
+          // rescaled rarely. The O update itself happens after P is stored.
+          float alpha = 1.0f;
+          bool need = false;
+          if (j == 0) {
+            m2 = mnew;
+          } else {
+            need = mnew > m2 + 8.0f;
+            if (need) {
+              alpha = ex2_approx(m2 - mnew);
+              l *= alpha;
+              m2 = mnew;
+            }
+          }
+          const float msub = (m2 == -INFINITY) ? 0.f : m2;
+          // exponentials, the row sum and the bf16 packing of P, two columns at a
+          // time with packed f32x2 arithmetic (half the FMA / add instructions)
+          uint32_t pk[BN / 2];
+          float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+          const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
+#pragma unroll
+          for (int c = 0; c < BN / 2; ++c) {
+            const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sl2x2, negm);
+            const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if (c & 1) ls1 = __fadd2_rn(ls1, p); else ls0 = __fadd2_rn(ls0, p);
+            pk[c] = pack_bf16x2(p.x, p.y);
+          }
+          {
+            const float2 ls = __fadd2_rn(ls0, ls1);
+            l += ls.x + ls.y;
+          }
+          // P_t(j) goes into columns 64..127 of the other tile's S once the scores
+          // there have been read: S_1(j) for tile 0, S_0(j+1) for tile 1 (whose
+          // computation followed O_1 += P_1(j-1) V, the last reader of those
+          // columns). Past the other tile's last key tile, wait for its last read
+          // and for this tile's previous O += P V instead.
+          {
+            const int other_nk = t ? nk[0] : nk[1];
+            const int want = j + t;  // tile 0: S_1(j); tile 1: S_0(j + 1)
+            bool w = true;
+            if (want < other_nk) {
+              w = mbar_wait_inl(bar(B_LOADED + (t ^ 1)), want & 1, ab, kDevErrTimeout);
+            } else {
+              if (other_nk > 0) w = mbar_wait_inl(bar(B_LOADED + (t ^ 1)), (other_nk - 1) & 1, ab, kDevErrTimeout);
+              if (w && j > 0) w = mbar_wait_inl(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout);
+            }
+            ok = __all_sync(FULL, w);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          tmem_st64(tP, pk);
+          if (__any_sync(FULL, need)) {
+            // O holds the sum up to tile j-1 once PV(t, j-1) has completed (S_t(j) was
+            // issued after it, so at most that one is in flight); PV(t, j) is not
+            // issued before this warpgroup arrives on PFULL below.
+            ok = __all_sync(FULL, mbar_wait_inl(bar(B_ODONE + t), (j - 1) & 1, ab, kDevErrTimeout));
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c4 = 0; c4 < HD / 32; ++c4) {
+              uint32_t rr[32];
+              tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+              tmem_st32(tO + static_cast<uint32_t>(32 * c4), rr);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(bar(B_PFULL + t));
+        }
+        if (ok && my_nk > 0) {
+          ok = __all_sync(FULL, mbar_wait_inl(bar(B_OFINAL + t), 0, ab, kDevErrTimeout));
+          if (ok) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            const bool store = qrow < row_end;
+            __nv_bfloat16* orow = a.out + static_cast<long long>(bi) * a.o_sb +
+                                  static_cast<long long>(qrow) * a.o_ss +
+                                  static_cast<long long>(h) * a.o_sh;
+#pragma unroll
+            for (int c4 = 0; c4 < HD / 32; ++c4) {
+              uint32_t rr[32];
+              tmem_ld32(tO + static_cast<uint32_t>(32 * c4), rr);
+              uint32_t pk[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                pk[e] = pack_bf16x2(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
+              if (store) {
+                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c4);
+#pragma unroll
+                for (int v4 = 0; v4 < 4; ++v4)
+                  dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+              }
+            }
+            if (a.lse != nullptr && store)
+              a.lse[(static_cast<long long>(bi) * a.Hq + h) * a.Sq + qrow] =
+                  (m2 + log2f(l)) * 0.69314718055994531f;
+          }
+        }
     }
   }
 
@@ -815,6 +836,13 @@ extern "C" int atf_prefill_fwd(const AtfPrefillParams* p, atf_stream_t stream) {
     return ATF_ERR_CUDA;
   const long long grid = static_cast<long long>(a.n_qblk) * a.B * a.Hq;
   if (grid > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
+  // setmaxnreg.inc waits until the block's launch registers cover the split:
+  // never launch a build whose register count would leave it waiting
+  static const int launch_regs = [] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, prefill_kernel) == cudaSuccess ? fa.numRegs : 0;
+  }();
+  if (static_cast<long long>(launch_regs) * THREADS < REG_SPLIT_TOTAL) return ATF_ERR_UNSUPPORTED;
   prefill_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES,
                    reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tkl, tv, a);
   return cudaGetLastError() == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
