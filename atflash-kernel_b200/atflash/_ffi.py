@@ -23,8 +23,8 @@ EXPORTED = ("atf_window_widths", "atf_window_zhi16", "atf_window_zhi8", "atf_win
             "atf_prefill_fwd", "atf_decode_plan", "atf_decode_run", "atf_decode_run_noalloc", "atf_lse_merge",
             "atf_rope_pack", "atf_paged_kv_append", "atf_status_string", "atf_version",
             "atf_read_error_flag", "atf_selftest_wait_timeout", "atf_params_size",
-            "atf_exchange_region_bytes", "atf_state_push", "atf_state_merge", "atf_ipc_export", "atf_ipc_import",
-            "atf_ipc_release")
+            "atf_exchange_region_bytes", "atf_state_push", "atf_state_merge", "atf_decode_run_exchange",
+            "atf_ipc_export", "atf_ipc_import", "atf_ipc_release")
 ATF_IPC_HANDLE_BYTES = 64
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -151,6 +151,7 @@ def load() -> ctypes.CDLL:
             lib.atf_exchange_region_bytes.argtypes = [_i32, _i32, _i32]
             lib.atf_state_push.argtypes = [P(AtfExchangeParams), _vp]
             lib.atf_state_merge.argtypes = [P(AtfExchangeParams), _vp]
+            lib.atf_decode_run_exchange.argtypes = [P(AtfDecodeParams), P(AtfExchangeParams), _vp]
             lib.atf_ipc_export.argtypes = [_vp, _vp, P(_i64)]
             lib.atf_ipc_import.argtypes = [_vp, _i64, P(_vp), P(_vp)]
             lib.atf_ipc_release.argtypes = [_vp]

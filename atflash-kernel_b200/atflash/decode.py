@@ -205,9 +205,14 @@ class BatchDecodeWithPagedKVCacheWrapper:
             out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
             return_lse: bool = False, enable_pdl=None, window_left=None,
             q_pos: Optional[torch.Tensor] = None, kv_pos0: Optional[torch.Tensor] = None,
-            out_dtype: Optional[torch.dtype] = None):
+            out_dtype: Optional[torch.dtype] = None, exchange=None):
         """q (B, Hq, 128) bf16; paged_kv_cache = (k_pages, v_pages) or one tensor with
-        a k/v axis at dim 1. Returns out (B, Hq, 128) [, lse (B, Hq), natural log]."""
+        a k/v axis at dim 1. Returns out (B, Hq, 128) [, lse (B, Hq), natural log].
+
+        With `exchange` (an atflash.dist.StateExchange whose ranks run on
+        different GPUs) this is one KV-sharded step: the decode's split merge also
+        exchanges the ranks' states (atf_decode_run_exchange), and out / lse are
+        the merge over every rank of the exchange."""
         if self._plan is None:
             raise RuntimeError("plan() must be called before run()")
         if q_scale is not None or k_scale is not None or v_scale is not None:
@@ -279,6 +284,13 @@ class BatchDecodeWithPagedKVCacheWrapper:
         if k_level_major:
             a.k_level_major = 1
             a.k_stride_page, a.k_stride_head, a.k_stride_level = kc.stride(0), kc.stride(1), kc.stride(2)
+        if exchange is not None:
+            x = exchange._fused_params(dev)
+            with torch.cuda.device(dev):
+                rc = _ffi.load().atf_decode_run_exchange(ctypes.byref(a), ctypes.byref(x),
+                                                         _runtime.stream_handle(dev))
+            _ffi.check("atf_decode_run_exchange", rc)
+            return (out, lse) if return_lse else out
         with torch.cuda.device(dev):
             rc = _ffi.load().atf_decode_run(ctypes.byref(a), _runtime.stream_handle(dev))
         _ffi.check("atf_decode_run", rc)

@@ -258,6 +258,7 @@ class StateExchange:
         self.base = (self._region.data_ptr() + 255) // 256 * 256
         self._opened = []
         self.peer_base = None
+        self._emulated = _emulate is not None
         if _emulate is not None:
             return  # peers are set by emulated()
         ptrs = [self.base]
@@ -310,6 +311,22 @@ class StateExchange:
         p.error_flag = _runtime.error_flag(self.device).data_ptr()
         return p
 
+    def _fused_params(self, device):
+        """The exchange fields atf_decode_run_exchange reads. Emulated ranks share
+        one GPU, and a fused step waits inside its kernel for the other ranks'
+        kernels, which on one GPU need not run at the same time: refused."""
+        from . import _ffi, _runtime
+        if self._emulated:
+            raise RuntimeError("an emulated exchange runs push() and merge() as separate steps; the fused "
+                               "decode step needs every rank on its own GPU")
+        if torch.device(device) != self.device:
+            raise ValueError("the decode runs on another device than the exchange region")
+        p = _ffi.AtfExchangeParams()
+        p.batch, p.num_heads, p.world, p.rank = self.B, self.H, self.world, self.rank
+        p.peer_base, p.base = self.peer_base.data_ptr(), self.base
+        p.error_flag = _runtime.error_flag(self.device).data_ptr()
+        return p
+
     def push(self, o: torch.Tensor, lse: torch.Tensor) -> None:
         """Send this rank's state (O fp32 (B, H, 128), LSE natural log (B, H))."""
         import ctypes
@@ -357,6 +374,10 @@ def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Ten
     all-gather of the ranks' states."""
     _, world = _rank_world(group)
     if exchange is not None:
+        if not exchange._emulated:
+            # one kernel after the decode merges, exchanges and merges again
+            return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                               out_dtype=out_dtype, exchange=exchange)
         B, H, D = q.shape
         o = torch.empty((B, H, D), dtype=torch.float32, device=q.device)
         lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
@@ -408,6 +429,11 @@ class ShardedDecodeStep:
         from .decode import lse_merge
 
         def local():
+            if exchange is not None and not exchange._emulated:
+                # the whole step in one graph: the decode and one kernel that
+                # merges its split, exchanges with the peers and merges again
+                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                                   out_dtype=out_dtype, exchange=exchange)
             if exchange is not None:
                 # the whole step (decode, push to the peers, merge) in one graph:
                 # no collective library call, the step counter is on the device

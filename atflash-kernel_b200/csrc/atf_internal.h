@@ -26,4 +26,8 @@ int check_device(int* device_out);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// atf_decode_run's checks and its split-KV kernel launch, without the merge
+// (decode.cu); atf_decode_run and atf_decode_run_exchange add their merges.
+int decode_launch_split(const AtfDecodeParams* p, cudaStream_t st);
+
 }  // namespace atf

@@ -1034,7 +1034,9 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
   return ATF_OK;
 }
 
-extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
+// Validates an atf_decode_run call and launches its split-KV kernel (none when
+// the plan has no items); the caller launches the merge that follows.
+int atf::decode_launch_split(const AtfDecodeParams* p, cudaStream_t st) {
   if (p == nullptr || p->q == nullptr || p->k_cache == nullptr || p->v_cache == nullptr ||
       p->indptr == nullptr || p->indices == nullptr || p->last_page_len == nullptr ||
       p->items == nullptr || p->item_indptr == nullptr || p->partial_o == nullptr ||
@@ -1066,7 +1068,6 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
   int dev = 0;
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int ps = p->page_size;
   const bool tma_path = (ps == 16 || ps == 32 || ps == 64 || ps == 128 || ps == 256) &&
                         p->qk_layout == ATF_LAYOUT_SORTED_PAIR && p->window != ATF_WINDOW_VEC8 &&
@@ -1160,25 +1161,16 @@ extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
     }
     if (cudaGetLastError() != cudaSuccess) return ATF_ERR_CUDA;
   }
-  merge::Args m;
-  m.part_stride_o = 0;
-  m.part_stride_l = 0;
-  m.po = p->partial_o;
-  m.pl = p->partial_lse;
-  m.indptr = p->item_indptr;
-  m.max_part = p->num_items;
-  m.P = 0;
-  m.B = p->batch_size;
-  m.H = p->num_qo_heads;
-  m.lse_log2 = 1;
-  m.out = p->out;
-  m.o_sb = p->o_stride_b;
-  m.o_sh = p->o_stride_h;
-  m.out_f32 = p->out_dtype == ATF_DTYPE_F32 ? 1 : 0;
-  m.lse_out = p->lse_out;
+  return ATF_OK;
+}
+
+extern "C" int atf_decode_run(const AtfDecodeParams* p, atf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int rc = decode_launch_split(p, st);
+  if (rc != ATF_OK) return rc;
   // launched as a programmatic dependent of the decode kernel: its launch
   // overlaps the decode's last wave, and it waits for the decode to complete
-  return merge::launch(m, st, /*after_decode=*/p->num_items > 0);
+  return merge::launch(merge::decode_merge_args(p), st, /*after_decode=*/p->num_items > 0);
 }
 
 extern "C" int atf_lse_merge(const AtfMergeParams* p, atf_stream_t stream) {

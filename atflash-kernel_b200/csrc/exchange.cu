@@ -57,10 +57,6 @@ struct PushArgs {
 
 constexpr int PUSH_WARPS = 8;
 
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 // One warp per (request, head) row of the state: a lane moves 4 of the 128
 // dims to every rank's slot; the block that finishes last signals every rank.
 __global__ void __launch_bounds__(PUSH_WARPS * 32) push_kernel(const PushArgs a) {
@@ -89,7 +85,7 @@ __global__ void __launch_bounds__(PUSH_WARPS * 32) push_kernel(const PushArgs a)
       for (int q = 0; q < a.W; ++q) {
         unsigned long long* flags =
             reinterpret_cast<unsigned long long*>(static_cast<char*>(a.peer_base[q]) + a.flags_off);
-        st_release_sys_u64(flags + a.rank, target);
+        merge::st_release_sys_u64(flags + a.rank, target);
       }
     }
   }
@@ -183,6 +179,31 @@ extern "C" int atf_state_merge(const AtfExchangeParams* p, atf_stream_t stream) 
   m.parity_stride = static_cast<long long>(p->world) * L.S;
   m.err = p->error_flag;
   return merge::launch(m, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int atf_decode_run_exchange(const AtfDecodeParams* p, const AtfExchangeParams* x,
+                                       atf_stream_t stream) {
+  if (p == nullptr || x == nullptr || x->peer_base == nullptr || x->base == nullptr) return ATF_ERR_INVALID_ARG;
+  if (x->world < 1 || x->world > 64 || x->rank < 0 || x->rank >= x->world || x->batch != p->batch_size ||
+      x->num_heads != p->num_qo_heads)
+    return ATF_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(x->base) & 255) return ATF_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int rc = decode_launch_split(p, st);
+  if (rc != ATF_OK) return rc;
+  const exchange::Layout L = exchange::layout(x->batch, x->num_heads, x->world);
+  merge::XArgs a;
+  a.local = merge::decode_merge_args(p);
+  a.peer_base = x->peer_base;
+  a.base = static_cast<char*>(x->base);
+  a.S = L.S;
+  a.flags_off = L.flags_off;
+  a.epoch_off = L.epoch_off;
+  a.tickets_off = L.tickets_off;
+  a.W = x->world;
+  a.rank = x->rank;
+  a.err = x->error_flag != nullptr ? x->error_flag : p->error_flag;
+  return merge::launch_exchange(a, st, /*after_decode=*/p->num_items > 0);
 }
 
 extern "C" int atf_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {

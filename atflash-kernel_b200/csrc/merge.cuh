@@ -56,60 +56,25 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
-static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
+// Merges the n parts of one (request, head) row: part i has its LSE at
+// pl[lb + i * sl] (log2 when lse_log2, else natural log) and its O at
+// po + ob + i * so. Every thread of the block calls it; the result is in warp
+// 0: lane l holds O dims 4l..4l+3 (normalised) in *o, and *lse is the row's
+// LSE (natural log; -inf when no part has weight).
+__device__ __forceinline__ void merge_row(const float* po, const float* pl, long long lb, long long sl,
+                                          long long ob, long long so, int n, int lse_log2, float4* o,
+                                          float* lse) {
   __shared__ float s_red[MERGE_WARPS];
   __shared__ float4 s_acc[MERGE_WARPS][32];
   __shared__ float s_l[MERGE_WARPS];
-  __shared__ unsigned long long s_target;
-  const int bh = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = bh / a.H, h = bh % a.H;
-  // launched as a programmatic dependent of the decode kernel: wait until that
-  // grid has completed and its partial states are visible (immediate otherwise)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const float* po = a.po;
-  const float* pl = a.pl;
-  if (a.wait_flags != nullptr) {
-    if (threadIdx.x == 0) {
-      const unsigned long long target = *reinterpret_cast<volatile unsigned long long*>(a.epoch) + 1ull;
-      s_target = target;
-      // bounded: a rank that never pushes leaves the error flag set
-      const uint64_t t0 = globaltimer_ns();
-      for (int q = 0; q < a.P; ++q) {
-        while (ld_acquire_sys_u64(a.wait_flags + q) < target) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            if (a.err != nullptr) atomicCAS(a.err, 0, kDevErrTimeout);
-            break;
-          }
-        }
-      }
-    }
-    __syncthreads();
-    const long long par = static_cast<long long>(s_target & 1ull) * a.parity_stride;
-    po += par;
-    pl += par;
-  }
-  int p0, p1;
-  // part i of this (b, h): O at po + ob + i * so, LSE at pl[lb + i * sl] (floats)
-  long long lb, sl, ob, so;
-  if (a.indptr != nullptr) {
-    p0 = min(max(a.indptr[b], 0), a.max_part);
-    p1 = min(max(a.indptr[b + 1], p0), a.max_part);
-    lb = static_cast<long long>(p0) * a.H + h;
-    sl = a.H;
-    ob = lb * 128;
-    so = sl * 128;
-  } else {
-    p0 = 0;
-    p1 = a.P;
-    lb = static_cast<long long>(b) * a.H + h;
-    ob = lb * 128;
-    sl = a.part_stride_l > 0 ? a.part_stride_l : static_cast<long long>(a.B) * a.H;
-    so = a.part_stride_o > 0 ? a.part_stride_o : static_cast<long long>(a.B) * a.H * 128;
-  }
-  const int n = p1 - p0;
-  const float cvt = a.lse_log2 ? 1.0f : 1.4426950408889634f;  // to log2
+  // a previous call's readers of the shared arrays are done
+  __syncthreads();
+  const float cvt = lse_log2 ? 1.0f : 1.4426950408889634f;  // to log2
   float M = -INFINITY;
   for (int i = threadIdx.x; i < n; i += MERGE_WARPS * 32) M = fmaxf(M, pl[lb + i * sl] * cvt);
 #pragma unroll
@@ -171,19 +136,87 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Ar
       L += s_l[w];
     }
     const float inv = L > 0.f ? 1.0f / L : 0.f;
-    const long long o = static_cast<long long>(b) * a.o_sb + static_cast<long long>(h) * a.o_sh + lane * 4;
-    if (a.out_f32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o) =
-          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    } else {
-      uint2 pk;
-      pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + o) = pk;
-    }
-    if (a.lse_out != nullptr && lane == 0)
-      a.lse_out[static_cast<long long>(b) * a.H + h] = L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
+    *o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    *lse = L > 0.f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
   }
+}
+
+// warp 0 of the row's block: O (fp32 or bf16) and the optional LSE
+__device__ __forceinline__ void store_row(void* out, long long o_off, int out_f32, float* lse_out,
+                                          long long row, float4 o, float lse) {
+  const int lane = threadIdx.x & 31;
+  if (out_f32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(out) + o_off + lane * 4) = o;
+  } else {
+    uint2 pk;
+    pk.x = pack_bf16x2(o.x, o.y);
+    pk.y = pack_bf16x2(o.z, o.w);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + o_off + lane * 4) = pk;
+  }
+  if (lse_out != nullptr && lane == 0) lse_out[row] = lse;
+}
+
+// ragged parts of request b: the items [indptr[b], indptr[b+1]), clamped to
+// [0, max_part)
+__device__ __forceinline__ void ragged_parts(const Args& a, int b, int h, int* n, long long* lb,
+                                             long long* sl, long long* ob, long long* so) {
+  const int p0 = min(max(a.indptr[b], 0), a.max_part);
+  const int p1 = min(max(a.indptr[b + 1], p0), a.max_part);
+  *n = p1 - p0;
+  *lb = static_cast<long long>(p0) * a.H + h;
+  *sl = a.H;
+  *ob = *lb * 128;
+  *so = *sl * 128;
+}
+
+static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Args a) {
+  __shared__ unsigned long long s_target;
+  const int bh = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int b = bh / a.H, h = bh % a.H;
+  // launched as a programmatic dependent of the decode kernel: wait until that
+  // grid has completed and its partial states are visible (immediate otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const float* po = a.po;
+  const float* pl = a.pl;
+  if (a.wait_flags != nullptr) {
+    if (threadIdx.x == 0) {
+      const unsigned long long target = *reinterpret_cast<volatile unsigned long long*>(a.epoch) + 1ull;
+      s_target = target;
+      // bounded: a rank that never pushes leaves the error flag set
+      const uint64_t t0 = globaltimer_ns();
+      for (int q = 0; q < a.P; ++q) {
+        while (ld_acquire_sys_u64(a.wait_flags + q) < target) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (a.err != nullptr) atomicCAS(a.err, 0, kDevErrTimeout);
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const long long par = static_cast<long long>(s_target & 1ull) * a.parity_stride;
+    po += par;
+    pl += par;
+  }
+  int n;
+  // part i of this (b, h): O at po + ob + i * so, LSE at pl[lb + i * sl] (floats)
+  long long lb, sl, ob, so;
+  if (a.indptr != nullptr) {
+    ragged_parts(a, b, h, &n, &lb, &sl, &ob, &so);
+  } else {
+    n = a.P;
+    lb = static_cast<long long>(b) * a.H + h;
+    ob = lb * 128;
+    sl = a.part_stride_l > 0 ? a.part_stride_l : static_cast<long long>(a.B) * a.H;
+    so = a.part_stride_o > 0 ? a.part_stride_o : static_cast<long long>(a.B) * a.H * 128;
+  }
+  float4 o;
+  float lse;
+  merge_row(po, pl, lb, sl, ob, so, n, a.lse_log2, &o, &lse);
+  if (warp == 0)
+    store_row(a.out, static_cast<long long>(b) * a.o_sb + static_cast<long long>(h) * a.o_sh, a.out_f32,
+              a.lse_out, static_cast<long long>(b) * a.H + h, o, lse);
   if (a.wait_flags != nullptr) {
     // the block that finishes last (all blocks have read the step's epoch and
     // parts) advances the step counter for the next exchange
@@ -198,6 +231,135 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Ar
       }
     }
   }
+}
+
+// The split-KV merge of a KV-sharded decode step fused with the cross-rank
+// exchange: one kernel after the decode, no collective. Per (request, head)
+// row, one block
+//   1. merges this rank's split-KV parts into its state of the row (the
+//      arithmetic of merge_kernel on the ragged parts),
+//   2. stores that state into slot [step parity][rank] of every rank's
+//      exchange region with peer stores (its own region included); the block
+//      that finishes this last signals every rank with a release store of the
+//      step,
+//   3. waits (bounded) for every peer's signal of the step; its own row of
+//      slot [rank] it wrote itself, so no block waits for another block of
+//      this grid,
+//   4. merges the ranks' states of the row in rank order (the arithmetic of
+//      merge_kernel on uniform parts) into the output.
+// The outputs are therefore bit-identical to the decode's merge, the push of
+// its state and the exchange merge run as three kernels. The block that
+// finishes last advances the step counter. Exchange region layout: the
+// slots, flags, step counter and tickets of exchange.cu.
+struct XArgs {
+  Args local;              // this rank's split-KV parts (ragged, LSE log2) and the output
+  void* const* peer_base;  // [W] every rank's exchange region as mapped here
+  char* base;              // this rank's region
+  long long S;             // floats per state
+  long long flags_off, epoch_off, tickets_off;  // bytes into a region
+  int W, rank;
+  int* err;
+};
+
+static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_exchange_kernel(const XArgs x) {
+  const Args& a = x.local;
+  __shared__ unsigned long long s_target;
+  const int bh = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = bh / a.H, h = bh % a.H;
+  const long long rows = static_cast<long long>(a.B) * a.H;
+  // a programmatic dependent of the decode kernel: its partial states are
+  // complete and visible past this point
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  unsigned long long* epoch = reinterpret_cast<unsigned long long*>(x.base + x.epoch_off);
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(x.base + x.tickets_off);
+  const unsigned long long* flags = reinterpret_cast<const unsigned long long*>(x.base + x.flags_off);
+  if (threadIdx.x == 0) s_target = *reinterpret_cast<volatile unsigned long long*>(epoch) + 1ull;
+  __syncthreads();
+  const unsigned long long target = s_target;
+  // 1. this rank's state of row (b, h)
+  int n;
+  long long lb, sl, ob, so;
+  ragged_parts(a, b, h, &n, &lb, &sl, &ob, &so);
+  float4 o;
+  float lse;
+  merge_row(a.po, a.pl, lb, sl, ob, so, n, a.lse_log2, &o, &lse);
+  // 2. into slot [target & 1][rank] of every rank's region
+  const long long slot = (static_cast<long long>(target & 1ull) * x.W + x.rank) * x.S;
+  if (warp == 0) {
+    for (int q = 0; q < x.W; ++q) {
+      float* dst = static_cast<float*>(x.peer_base[q]) + slot;
+      *reinterpret_cast<float4*>(dst + static_cast<long long>(bh) * 128 + lane * 4) = o;
+      if (lane == 0) dst[rows * 128 + bh] = lse;
+    }
+  }
+  // warp 0's stores are visible system-wide before the block's ticket
+  if (warp == 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int t = atomicAdd(tickets, 1u);
+    if (t + 1 == gridDim.x) {
+      *tickets = 0u;
+      __threadfence_system();
+      for (int q = 0; q < x.W; ++q) {
+        unsigned long long* f =
+            reinterpret_cast<unsigned long long*>(static_cast<char*>(x.peer_base[q]) + x.flags_off);
+        st_release_sys_u64(f + x.rank, target);
+      }
+    }
+    // 3. bounded: a rank that never pushes leaves the error flag set
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < x.W; ++q) {
+      if (q == x.rank) continue;
+      while (ld_acquire_sys_u64(flags + q) < target) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (x.err != nullptr) atomicCAS(x.err, 0, kDevErrTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // 4. the ranks' states of this step's parity, in rank order
+  const float* po = reinterpret_cast<const float*>(x.base) + static_cast<long long>(target & 1ull) * x.W * x.S;
+  merge_row(po, po + rows * 128, bh, x.S, static_cast<long long>(bh) * 128, x.S, x.W, /*lse_log2=*/0, &o, &lse);
+  if (warp == 0)
+    store_row(a.out, static_cast<long long>(b) * a.o_sb + static_cast<long long>(h) * a.o_sh, a.out_f32,
+              a.lse_out, bh, o, lse);
+  // 5. the block that finishes last (every block has read the step's epoch
+  // and its parts) advances the step counter
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int t = atomicAdd(tickets + 1, 1u);
+    if (t + 1 == gridDim.x) {
+      tickets[1] = 0u;
+      *reinterpret_cast<volatile unsigned long long*>(epoch) = target;
+      __threadfence();
+    }
+  }
+}
+
+// The split-KV merge of atf_decode_run: the ragged parts of each request
+// (LSE in log2) into the caller's output.
+inline Args decode_merge_args(const AtfDecodeParams* p) {
+  Args m;
+  m.part_stride_o = 0;
+  m.part_stride_l = 0;
+  m.po = p->partial_o;
+  m.pl = p->partial_lse;
+  m.indptr = p->item_indptr;
+  m.max_part = p->num_items;
+  m.P = 0;
+  m.B = p->batch_size;
+  m.H = p->num_qo_heads;
+  m.lse_log2 = 1;
+  m.out = p->out;
+  m.o_sb = p->o_stride_b;
+  m.o_sh = p->o_stride_h;
+  m.out_f32 = p->out_dtype == ATF_DTYPE_F32 ? 1 : 0;
+  m.lse_out = p->lse_out;
+  return m;
 }
 
 // after_decode: launch with programmatic stream serialization, so that the
@@ -221,6 +383,22 @@ static int launch(const Args& a, cudaStream_t stream, bool after_decode = false)
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, merge_kernel, a) == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
+}
+
+static int launch_exchange(const XArgs& x, cudaStream_t stream, bool after_decode) {
+  const long long blocks = static_cast<long long>(x.local.B) * x.local.H;
+  if (blocks > 0x7fffffffLL) return ATF_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(MERGE_WARPS * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_decode ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, merge_exchange_kernel, x) == cudaSuccess ? ATF_OK : ATF_ERR_CUDA;
 }
 
 }  // namespace merge

@@ -622,11 +622,23 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
             xstep = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
             ms_xg, _ = timed(lambda i: xstep(), steps, warmup, world)
             xstep.release()
+            # the same exchange as three kernels after the decode (its split merge,
+            # atf_state_push, atf_state_merge), eager: what the fused kernel replaces
+            o3 = torch.empty((B, hq, D), dtype=torch.float32, device=device)
+            l3 = torch.empty((B, hq), dtype=torch.float32, device=device)
+
+            def three(i):
+                w.run(q, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, out=o3, lse=l3, return_lse=True,
+                      out_dtype=torch.float32)
+                ex.push(o3, l3)
+                ex.merge(o3, l3)
+            ms_x3, _ = timed(three, steps, warmup, world)
             barrier(world)
             ex.close()
             barrier(world)
             res[name]["us_exchange"] = ms_x * 1e3
             res[name]["us_exchange_graph"] = ms_xg * 1e3
+            res[name]["us_exchange_three_kernels"] = ms_x3 * 1e3
             res[name]["gbs_aggregate_exchange_graph"] = total / (ms_xg * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
     res["parity"] = decode_1m_parity(device, rank, world, q, (kc, vc), kc_lm, perm, q_pos, kv_pos0, N, shard,
@@ -635,7 +647,9 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
                      f"NHD K pages), KV split into {world} shards, "
                      "all-gather of (O, LSE) + LSE merge inside the step; us: eager "
                      "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep; us_exchange(_graph): "
-                     "the states exchanged by NVLink peer stores (atflash.dist.StateExchange), no collective")
+                     "the states exchanged by NVLink peer stores (atflash.dist.StateExchange), no collective, in one "
+                     "kernel with the decode's split merge (atf_decode_run_exchange); us_exchange_three_kernels: the "
+                     "same exchange as the split merge, atf_state_push and atf_state_merge")
     del kc, vc, kc_lm
     torch.cuda.empty_cache()
     return res
@@ -666,7 +680,8 @@ def decode_1m_parity(device, rank, world, q, cache, k_lm, perm, q_pos, kv_pos0, 
     (ref_window_attn phase="decode", every key). Several ranks: rank 0 decodes
     every rank's shard on its own GPU (the shards regenerated from the ranks'
     seeds), merges the partial states with the same LSE merge, and checks that
-    the sharded step's result is bit-identical to this single-GPU emulation."""
+    the sharded step's result is bit-identical to this single-GPU emulation,
+    through the NCCL all-gather and through the fused peer-store exchange."""
     import atflash
     hq, hkv = q.shape[1], cache[0].shape[2]
     G = hq // hkv
@@ -679,6 +694,15 @@ def decode_1m_parity(device, rank, world, q, cache, k_lm, perm, q_pos, kv_pos0, 
                hq, hkv, D, page, window_table=wt, q_pos=q_pos, kv_pos0=kv_pos0)
         o, l = atflash.dist.sharded_decode(q, w, (k_lm, cache[1]), q_pos=q_pos, kv_pos0=kv_pos0)
         torch.cuda.synchronize()
+        if world > 1:
+            # the same step with the states exchanged by NVLink peer stores, fused
+            # into the decode's split merge (atf_decode_run_exchange)
+            ex = atflash.dist.StateExchange(1, hq)
+            ox, lx = atflash.dist.sharded_decode(q, w, (k_lm, cache[1]), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
+            torch.cuda.synchronize()
+            barrier(world)
+            ex.close()
+            barrier(world)
         if rank == 0 and world == 1:
             from oracle import attention as OA
             from oracle import window_table as OWT
@@ -710,8 +734,10 @@ def decode_1m_parity(device, rank, world, q, cache, k_lm, perm, q_pos, kv_pos0, 
             eo, el = atflash.lse_merge(torch.stack(po), torch.stack(pl), lse_log2=False, out_dtype=o.dtype,
                                        return_lse=True)
             torch.cuda.synchronize()
-            good = torch.equal(eo.view(torch.int16), o.view(torch.int16)) and torch.equal(el, l)
-            out[name] = {"bit_equal_single_gpu_emulation": good}
+            good_ag = torch.equal(eo.view(torch.int16), o.view(torch.int16)) and torch.equal(el, l)
+            good_ex = torch.equal(eo.view(torch.int16), ox.view(torch.int16)) and torch.equal(el, lx)
+            good = good_ag and good_ex
+            out[name] = {"bit_equal_single_gpu_emulation": good_ag, "exchange_bit_equal_single_gpu_emulation": good_ex}
         else:
             good = True
         ok = ok and good

@@ -311,6 +311,18 @@ int64_t atf_exchange_region_bytes(int32_t batch, int32_t num_heads, int32_t worl
 int atf_state_push(const AtfExchangeParams* p, atf_stream_t stream);
 /* Wait (bounded) for every rank's push of this step, merge, advance the step. */
 int atf_state_merge(const AtfExchangeParams* p, atf_stream_t stream);
+/* One KV-sharded decode step with the exchange fused into the decode's own
+ * split merge: atf_decode_run(p) whose merge kernel also stores this rank's
+ * state into every rank's region (as atf_state_push), waits (bounded) for
+ * every peer's state of the step and writes the merge of all ranks' states to
+ * p->out / p->lse_out (as atf_state_merge). One kernel follows the decode
+ * instead of three; the outputs are bit-identical to atf_decode_run with fp32
+ * out and lse, atf_state_push and atf_state_merge. Uses x's batch, num_heads,
+ * world, rank, peer_base, base and error_flag (p->error_flag when NULL); x's
+ * o, lse and out fields are not read. Every rank of the exchange calls it once
+ * per step; the ranks of one exchange must run on different GPUs, since each
+ * rank's kernel waits for the others'. */
+int atf_decode_run_exchange(const AtfDecodeParams* p, const AtfExchangeParams* x, atf_stream_t stream);
 /* CUDA IPC of a device allocation: the handle of the allocation holding dev_ptr
  * and dev_ptr's offset in it; import maps a peer's handle (ptr = base + offset);
  * release unmaps a base returned by import. Setup calls, not for the step loop. */

@@ -7,7 +7,8 @@ the partial (O, LSE) are all-gathered and merged; the result must match the
 one-GPU decode of the whole cache (same kernels, different split points, so a
 tolerance rather than bit equality). The NVLink state exchange (peer stores, no
 collective) must equal the all-gather path bit for bit, eagerly and replayed
-from a CUDA graph."""
+from a CUDA graph, both as the fused step (atf_decode_run_exchange) and as the
+decode's merge followed by separate push and merge kernels."""
 import os
 import socket
 
@@ -126,6 +127,19 @@ def _worker(rank, world, port, errq):
         torch.cuda.synchronize()
         assert torch.equal(og, out2) and torch.equal(lg, lse2), "graph-replayed exchange step differs"
         gstep.release()
+        # the separate-kernel path on the same exchange (decode merge, push,
+        # merge): the same bits, and the step protocol carries on between the two
+        for _ in range(2):
+            o_s, l_s = w2.run(step.q, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                              out_dtype=torch.float32)
+            ex.push(o_s, l_s)
+            os_, ls_ = ex.merge(o_s, l_s, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.equal(os_, out2) and torch.equal(ls_, lse2), "push / merge kernels differ"
+            ox, lx = atflash.dist.sharded_decode(step.q, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                                 out_dtype=torch.float32, exchange=ex)
+            torch.cuda.synchronize()
+            assert torch.equal(ox, out2) and torch.equal(lx, lse2), "fused step after push / merge differs"
         assert atflash.check_device_errors() == 0
         dist.barrier()
         ex.close()

@@ -109,6 +109,7 @@ def test_invalid_arguments_rejected_without_gpu():
     assert lib.atf_rope_pack(ctypes.byref(r), None) == -1  # in place
     assert lib.atf_state_push(None, None) == -1
     assert lib.atf_state_merge(None, None) == -1
+    assert lib.atf_decode_run_exchange(None, None, None) == -1
     x = _ffi.AtfExchangeParams()
     x.o = x.lse = x.peer_base = x.base = 256
     x.batch, x.num_heads, x.world, x.rank = 1, 28, 2, 2  # rank outside the group
@@ -120,6 +121,17 @@ def test_invalid_arguments_rejected_without_gpu():
     S = 28 * 128 + 28
     assert lib.atf_exchange_region_bytes(1, 28, 8) == ((2 * 8 * S * 4 + 8 * 8 + 8 + 8) + 255) // 256 * 256
     assert lib.atf_exchange_region_bytes(0, 28, 8) == -1
+    # the fused decode step: the exchange must match the decode's batch and heads
+    d = _ffi.AtfDecodeParams()
+    d.q = d.k_cache = d.v_cache = d.indptr = d.indices = d.last_page_len = 256
+    d.items = d.item_indptr = d.partial_o = d.partial_lse = d.out = 256
+    d.head_dim, d.batch_size, d.num_qo_heads, d.num_kv_heads, d.page_size = 128, 1, 28, 4, 16
+    x.base = 256
+    x.num_heads = 24
+    assert lib.atf_decode_run_exchange(ctypes.byref(d), ctypes.byref(x), None) == -1
+    x.num_heads = 28
+    x.base = 272
+    assert lib.atf_decode_run_exchange(ctypes.byref(d), ctypes.byref(x), None) == -3
 
 
 def test_decode_run_rejects_misaligned_workspace_and_output():
