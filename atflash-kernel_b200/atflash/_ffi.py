@@ -72,7 +72,7 @@ class AtfDecodeParams(ctypes.Structure):
                 ("o_stride_b", _i64), ("o_stride_h", _i64), ("out_dtype", ctypes.c_int),
                 ("lse_out", _vp), ("error_flag", _vp),
                 ("k_level_major", ctypes.c_int), ("k_stride_page", _i64), ("k_stride_head", _i64),
-                ("k_stride_level", _i64)]
+                ("k_stride_level", _i64), ("enable_pdl", ctypes.c_int)]
 
 
 class AtfMergeParams(ctypes.Structure):

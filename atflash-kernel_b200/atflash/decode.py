@@ -209,6 +209,13 @@ class BatchDecodeWithPagedKVCacheWrapper:
         """q (B, Hq, 128) bf16; paged_kv_cache = (k_pages, v_pages) or one tensor with
         a k/v axis at dim 1. Returns out (B, Hq, 128) [, lse (B, Hq), natural log].
 
+        enable_pdl=True launches the decode as a programmatic dependent of the
+        previous kernel on the stream: its prologue (the plan and the page table:
+        items, indptr, indices, last_page_len) runs while that kernel finishes, and
+        everything else (q, q_pos, kv_pos0, the KV pages, the outputs) waits for
+        it. Leave it off when the kernel just before the decode writes the page
+        table. The results are the same either way.
+
         With `exchange` (an atflash.dist.StateExchange whose ranks run on
         different GPUs) this is one KV-sharded step: the decode's split merge also
         exchanges the ranks' states (atf_decode_run_exchange), and out / lse are
@@ -281,6 +288,10 @@ class BatchDecodeWithPagedKVCacheWrapper:
         a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
         a.out_dtype = _ffi.ATF_DTYPE_F32 if out.dtype == torch.float32 else _ffi.ATF_DTYPE_BF16
         a.lse_out = lse.data_ptr() if lse is not None else None
+        # programmatic dependent launch: the decode's prologue (plan and page
+        # table reads) overlaps the previous kernel on the stream; opt-in, since a
+        # kernel that writes the page table must not directly precede the decode
+        a.enable_pdl = 1 if enable_pdl else 0
         if k_level_major:
             a.k_level_major = 1
             a.k_stride_page, a.k_stride_head, a.k_stride_level = kc.stride(0), kc.stride(1), kc.stride(2)

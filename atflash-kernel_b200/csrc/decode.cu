@@ -171,6 +171,9 @@ __global__ void __launch_bounds__(THREADS, 2) decode_kernel(const Args a) {
   // the split merge that follows on the stream may be scheduled now; it waits
   // for this grid's completion before reading the partial states
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // under programmatic dependent launch: every input is read after the
+  // previous grid on the stream has completed (immediate otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -468,6 +471,9 @@ __global__ void __launch_bounds__(THREADS, 2)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int item = blockIdx.x, hk = blockIdx.y;
+  // Prologue, part 1: only the plan (items) and the page table, which no kernel
+  // of this step writes. Under programmatic dependent launch it runs while the
+  // previous kernel on the stream is still running.
   const int b = a.items[4 * item + 0];
   const int k_beg = a.items[4 * item + 1];
   const int k_end = a.items[4 * item + 2];
@@ -475,8 +481,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int npages = a.indptr[b + 1] - pg0;
   const long long kv_len =
       npages > 0 ? static_cast<long long>(npages - 1) * a.page_size + a.last_page_len[b] : 0;
-  const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
-  const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
   // an item (from atf_decode_plan) starts on a 64-key boundary, lies inside its
   // request and holds at most MAX_ITEM_KEYS keys (its page list is staged in
   // shared memory); any other item is reported and skipped
@@ -488,15 +492,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int G = a.G;
   const int hq0 = hk * G;
   const int nst = (k_end - k_beg + STAGE_KEYS - 1) / STAGE_KEYS;
-  int lim[ATF_MAX_LEVELS];
-#pragma unroll
-  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, q_pos - pos0, i);
-  // ring geometry of this item (the same in every role)
-  const int Lc = k_end > k_beg ? decode::levels_of(lim, k_end - 1) : ATF_MAX_LEVELS;
-  const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
-  const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
-  const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
-
   if (tid == 0) {
     *s_abort = (args.err != nullptr && *reinterpret_cast<volatile int*>(args.err) != 0) ? 1 : 0;
     for (int s = 0; s < NSTAGE_MAX; ++s) {
@@ -505,6 +500,30 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     fence_mbar_init();
   }
+  // the item's page list, staged once by the producer warp so that no TMA
+  // waits on a global load
+  int* s_pages = reinterpret_cast<int*>(sp + OFF_PAGES);
+  const int first_page = k_beg / a.page_size;
+  if (warp == CONSUMERS) {
+    if (lane < ATF_MAX_LEVELS) tma_prefetch_desc(&tmK.lv[lane]);
+    if (lane == ATF_MAX_LEVELS) tma_prefetch_desc(&tmV);
+    const int n_item_pages = k_end > k_beg ? (k_end - 1) / a.page_size - first_page + 1 : 0;
+    for (int i = lane; i < n_item_pages; i += 32) s_pages[i] = a.indices[pg0 + first_page + i];
+  }
+  // Part 2: what a preceding kernel may have written (the positions, the
+  // query, the KV pages) and this kernel's outputs come after the previous
+  // grid has completed (immediate without programmatic dependent launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
+  const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+  int lim[ATF_MAX_LEVELS];
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, q_pos - pos0, i);
+  // ring geometry of this item (the same in every role)
+  const int Lc = k_end > k_beg ? decode::levels_of(lim, k_end - 1) : ATF_MAX_LEVELS;
+  const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
+  const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
+  const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
   __syncthreads();
   const AbortCtl ab{s_abort, args.err};
   const bool start_ok = (*s_abort == 0);
@@ -522,14 +541,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (start_ok && warp == CONSUMERS) {
     // ------------------------------------------------------------ producer
     const int R = args.rows;
-    if (lane < ATF_MAX_LEVELS) tma_prefetch_desc(&tmK.lv[lane]);
-    if (lane == ATF_MAX_LEVELS) tma_prefetch_desc(&tmV);
-    // the item's page list, staged once so that no TMA waits on a global load
-    int* s_pages = reinterpret_cast<int*>(sp + OFF_PAGES);
-    const int first_page = k_beg / a.page_size;
-    const int n_item_pages = k_end > k_beg ? (k_end - 1) / a.page_size - first_page + 1 : 0;
-    for (int i = lane; i < n_item_pages; i += 32) s_pages[i] = a.indices[pg0 + first_page + i];
-    __syncwarp();
     int issued = 0;
     for (int s = 0; s < nst; ++s) {
       const int buf = s % NSTAGE;
@@ -1034,6 +1045,26 @@ extern "C" int atf_decode_plan(const AtfDecodePlanParams* p, int32_t* items_host
   return ATF_OK;
 }
 
+// A kernel launch, with programmatic stream serialization when `pdl`: the grid
+// may then start while the previous kernel on the stream is still running; the
+// decode kernels read only the plan and the page table before their
+// griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, uint32_t smem, cudaStream_t st,
+                              bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Validates an atf_decode_run call and launches its split-KV kernel (none when
 // the plan has no items); the caller launches the merge that follows.
 int atf::decode_launch_split(const AtfDecodeParams* p, cudaStream_t st) {
@@ -1152,12 +1183,16 @@ int atf::decode_launch_split(const AtfDecodeParams* p, cudaStream_t st) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_tma::SMEM_BYTES) !=
           cudaSuccess)
         return ATF_ERR_CUDA;
-      kern<<<grid, decode_tma::THREADS, decode_tma::SMEM_BYTES, st>>>(tk, tv, ta);
+      if (launch_pdl(kern, grid, decode_tma::THREADS, decode_tma::SMEM_BYTES, st, p->enable_pdl != 0, tk, tv,
+                     ta) != cudaSuccess)
+        return ATF_ERR_CUDA;
     } else {
       if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                decode::SMEM_BYTES) != cudaSuccess)
         return ATF_ERR_CUDA;
-      decode::decode_kernel<<<grid, decode::THREADS, decode::SMEM_BYTES, st>>>(a);
+      if (launch_pdl(decode::decode_kernel, grid, decode::THREADS, decode::SMEM_BYTES, st, p->enable_pdl != 0,
+                     a) != cudaSuccess)
+        return ATF_ERR_CUDA;
     }
     if (cudaGetLastError() != cudaSuccess) return ATF_ERR_CUDA;
   }

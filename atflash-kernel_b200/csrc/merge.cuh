@@ -174,6 +174,10 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_kernel(const Ar
   const int bh = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int b = bh / a.H, h = bh % a.H;
+  // a kernel launched after this one with programmatic dependent launch (the
+  // next decode step) may start its prologue now; it waits for this grid's
+  // completion before it reads anything this grid writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // launched as a programmatic dependent of the decode kernel: wait until that
   // grid has completed and its partial states are visible (immediate otherwise)
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -268,6 +272,9 @@ static __global__ void __launch_bounds__(MERGE_WARPS * 32) merge_exchange_kernel
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = bh / a.H, h = bh % a.H;
   const long long rows = static_cast<long long>(a.B) * a.H;
+  // the next decode step, when launched as a programmatic dependent, may start
+  // its prologue now (it waits for this grid before touching its outputs)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // a programmatic dependent of the decode kernel: its partial states are
   // complete and visible past this point
   asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -551,8 +551,15 @@ def bench_decode(device, steps, warmup, peaks, N=131072):
         zhi = wt.zhi16 if wt is not None else None
         byts = WT.decode_bytes(hkv, [N] * B, zhi)["bytes"]
         res[name] = {"us": ms * 1e3, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9}
+        if kk is kc_lm:
+            # the same steps launched with programmatic dependent launch: each
+            # decode's prologue overlaps the previous step's merge
+            ms_p, _ = timed(lambda i: w.run(q, (kk, vc), out=out, enable_pdl=True), steps, warmup, 1)
+            res[name]["us_pdl"] = ms_p * 1e3
+            res[name]["gbs_pdl"] = byts / (ms_p * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on"]["us"]
     res["hbm_frac_on"] = res["on"]["gbs"] / peaks["hbm_gbs"]
+    res["hbm_frac_on_pdl"] = res["on"]["gbs_pdl"] / peaks["hbm_gbs"]
     res["ratio_on_off_nhd_k"] = res["off_nhd_k"]["us"] / res["on_nhd_k"]["us"]
     res["hbm_frac_on_nhd_k"] = res["on_nhd_k"]["gbs"] / peaks["hbm_gbs"]
     del kc, vc, kc_lm

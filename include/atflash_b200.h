@@ -211,6 +211,13 @@ typedef struct {
    * layout, the 16-snap or no window and a page size of 16..256 (power of 2). */
   int k_level_major;
   int64_t k_stride_page, k_stride_head, k_stride_level; /* elements; the token stride is 16 */
+  /* Programmatic dependent launch (optional, 0 = off): the split kernel may
+   * start while the previous kernel on the stream is still running. Before it
+   * waits for that kernel it reads only items, item_indptr, indptr, indices and
+   * last_page_len, so a kernel that writes one of those must not directly
+   * precede the decode on the stream when this is set; q, q_pos, kv_pos0, the
+   * KV pages and the outputs are read or written after the wait. */
+  int enable_pdl;
 } AtfDecodeParams;
 
 /* Paged-KV GQA split-KV decode followed by the LSE merge of its splits. */

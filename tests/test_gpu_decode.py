@@ -362,3 +362,36 @@ def test_decode_level_major_k_pages_equal_nhd(cuda_device, page, k_ret):
     ref = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, window_table=wt)
     got = run_decode(cuda_device, q, _level_major(kc), vc, indptr, indices, lpl, hq, hkv, page, window_table=wt)
     assert torch.equal(ref, got)
+
+
+@pytest.mark.parametrize("qk_layout", ["sorted_pair", "rotate_half"])
+def test_decode_pdl_bit_identical(cuda_device, qk_layout):
+    """enable_pdl=True (the decode launched as a programmatic dependent of the
+    previous kernel) gives the plain launch's bits, on the TMA kernel (sorted
+    pairs) and on the general kernel (rotate_half), also when the kernel just
+    before the decode rewrites the query and a KV page: those are read after
+    the decode's wait for the previous grid."""
+    import atflash
+    kv_lens, hq, hkv, page = [3000, 700, 64], 24, 8, 16
+    q, kc, vc, indptr, indices, lpl, _, _ = make_paged(kv_lens, hq, hkv, page, seed=23)
+    q, kc, vc = q.to(cuda_device), kc.to(cuda_device), vc.to(cuda_device)
+    w = atflash.BatchDecodeWithPagedKVCacheWrapper(torch.empty(64 << 20, dtype=torch.uint8, device=cuda_device),
+                                                   "NHD")
+    w.plan(indptr, indices, lpl, hq, hkv, 128, page, window_table=atflash.WindowTable(128, 5e5, 2.0),
+           qk_layout=qk_layout)
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    out_p = torch.empty((len(kv_lens), hq, 128), dtype=torch.bfloat16, device=cuda_device)
+    pg = int(indices[5])
+    for step in range(3):
+        # kernels that write the decode's inputs, directly before each decode
+        q.copy_(torch.randn(q.shape, generator=g, device=cuda_device).to(torch.bfloat16))
+        kc[pg].mul_(-1.0)
+        w.run(q, (kc, vc), out=out_p, enable_pdl=True)
+        ref = w.run(q, (kc, vc))
+        torch.cuda.synchronize()
+        assert torch.equal(out_p.view(torch.int16), ref.view(torch.int16)), step
+    # back to back, the next decode launched while the previous merge runs
+    outs = [w.run(q, (kc, vc), enable_pdl=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(o.view(torch.int16), ref.view(torch.int16)) for o in outs)
+    assert atflash.check_device_errors() == 0
