@@ -366,33 +366,37 @@ class StateExchange:
 
 def sharded_decode(q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
                    kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16,
-                   exchange: Optional[StateExchange] = None):
+                   exchange: Optional[StateExchange] = None, enable_pdl: bool = False):
     """Decode with this rank's KV shard; `wrapper` is planned over the rank's local
     pages. q_pos: global query position per request; kv_pos0: global position of
     this rank's first key per request. Returns (out, lse) merged over the group:
     through `exchange` (peer stores, no collective) when given, else with one
-    all-gather of the ranks' states."""
+    all-gather of the ranks' states. enable_pdl: the decode's launch as in
+    BatchDecodeWithPagedKVCacheWrapper.run."""
     _, world = _rank_world(group)
     if exchange is not None:
         if not exchange._emulated:
             # one kernel after the decode merges, exchanges and merges again
-            return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+            return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                               enable_pdl=enable_pdl, return_lse=True,
                                out_dtype=out_dtype, exchange=exchange)
         B, H, D = q.shape
         o = torch.empty((B, H, D), dtype=torch.float32, device=q.device)
         lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
-        wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=o, lse=lse, return_lse=True,
+        wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                    enable_pdl=enable_pdl, out=o, lse=lse, return_lse=True,
                     out_dtype=torch.float32)
         exchange.push(o, lse)
         return exchange.merge(o, lse, out_dtype=out_dtype)
     if world == 1:
         # one shard: the decode's own split merge is already the result
-        return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+        return wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, enable_pdl=enable_pdl, return_lse=True,
                            out_dtype=out_dtype)
     # the local state goes straight into the buffer that is all-gathered
     B, H, D = q.shape
     pack, o_view, l_view = _pack_views(B, H, D, q.device)
-    wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=o_view, lse=l_view, return_lse=True,
+    wrapper.run(q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                enable_pdl=enable_pdl, out=o_view, lse=l_view, return_lse=True,
                 out_dtype=torch.float32)
     return _gather_and_merge(pack, B, H, D, group, world, None, out_dtype)
 
@@ -413,7 +417,7 @@ class ShardedDecodeStep:
 
     def __init__(self, q: torch.Tensor, wrapper, paged_kv_cache, *, q_pos: torch.Tensor,
                  kv_pos0: torch.Tensor, group=None, out_dtype=torch.bfloat16,
-                 exchange: Optional["StateExchange"] = None):
+                 exchange: Optional["StateExchange"] = None, enable_pdl: bool = False):
         if not (q_pos.is_cuda and kv_pos0.is_cuda):
             raise ValueError("q_pos and kv_pos0 must be CUDA tensors (they are read by the replayed graph)")
         _, self.world = _rank_world(group)
@@ -432,19 +436,23 @@ class ShardedDecodeStep:
             if exchange is not None and not exchange._emulated:
                 # the whole step in one graph: the decode and one kernel that
                 # merges its split, exchanges with the peers and merges again
-                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                                   enable_pdl=enable_pdl, return_lse=True,
                                    out_dtype=out_dtype, exchange=exchange)
             if exchange is not None:
                 # the whole step (decode, push to the peers, merge) in one graph:
                 # no collective library call, the step counter is on the device
-                wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=self.o_view, lse=self.l_view,
+                wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                            enable_pdl=enable_pdl, out=self.o_view, lse=self.l_view,
                             return_lse=True, out_dtype=torch.float32)
                 exchange.push(self.o_view, self.l_view)
                 return exchange.merge(self.o_view, self.l_view, out_dtype=out_dtype)
             if self.world == 1:
-                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, return_lse=True,
+                return wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                                   enable_pdl=enable_pdl, return_lse=True,
                                    out_dtype=out_dtype)
-            wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0, out=self.o_view, lse=self.l_view,
+            wrapper.run(self.q, paged_kv_cache, q_pos=q_pos, kv_pos0=kv_pos0,
+                        enable_pdl=enable_pdl, out=self.o_view, lse=self.l_view,
                         return_lse=True, out_dtype=torch.float32)
             return None
 

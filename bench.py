@@ -619,6 +619,12 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
         step.release()
         res[name]["us_graph"] = ms_g * 1e3
         res[name]["gbs_aggregate_graph"] = total / (ms_g * 1e-3) / 1e9
+        if world == 1:
+            # the decode launched as a programmatic dependent of the previous step's merge
+            pstep = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, enable_pdl=True)
+            ms_gp, _ = timed(lambda i: pstep(), steps, warmup, world)
+            pstep.release()
+            res[name]["us_graph_pdl"] = ms_gp * 1e3
         if world > 1:
             # the same step with the ranks' states exchanged by NVLink peer stores
             # (atflash.dist.StateExchange) instead of the NCCL all-gather: eager,
@@ -629,6 +635,12 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
             xstep = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex)
             ms_xg, _ = timed(lambda i: xstep(), steps, warmup, world)
             xstep.release()
+            # and with each decode launched as a programmatic dependent of the
+            # previous step's exchange kernel (its prologue overlaps that wait)
+            pstep = atflash.dist.ShardedDecodeStep(q, w, (kk, vc), q_pos=q_pos, kv_pos0=kv_pos0, exchange=ex,
+                                                   enable_pdl=True)
+            ms_xgp, _ = timed(lambda i: pstep(), steps, warmup, world)
+            pstep.release()
             # the same exchange as three kernels after the decode (its split merge,
             # atf_state_push, atf_state_merge), eager: what the fused kernel replaces
             o3 = torch.empty((B, hq, D), dtype=torch.float32, device=device)
@@ -645,6 +657,7 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
             barrier(world)
             res[name]["us_exchange"] = ms_x * 1e3
             res[name]["us_exchange_graph"] = ms_xg * 1e3
+            res[name]["us_exchange_graph_pdl"] = ms_xgp * 1e3
             res[name]["us_exchange_three_kernels"] = ms_x3 * 1e3
             res[name]["gbs_aggregate_exchange_graph"] = total / (ms_xg * 1e-3) / 1e9
     res["ratio_on_off"] = res["off"]["us"] / res["on_k64"]["us"]
@@ -656,7 +669,8 @@ def bench_decode_1m(device, rank, world, steps, warmup, peaks, N=1 << 20):
                      "atflash.dist.sharded_decode, us_graph: atflash.dist.ShardedDecodeStep; us_exchange(_graph): "
                      "the states exchanged by NVLink peer stores (atflash.dist.StateExchange), no collective, in one "
                      "kernel with the decode's split merge (atf_decode_run_exchange); us_exchange_three_kernels: the "
-                     "same exchange as the split merge, atf_state_push and atf_state_merge")
+                     "same exchange as the split merge, atf_state_push and atf_state_merge; *_pdl: each decode launched as a "
+                     "programmatic dependent of the previous step's last kernel (enable_pdl)")
     del kc, vc, kc_lm
     torch.cuda.empty_cache()
     return res

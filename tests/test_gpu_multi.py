@@ -127,6 +127,14 @@ def _worker(rank, world, port, errq):
         torch.cuda.synchronize()
         assert torch.equal(og, out2) and torch.equal(lg, lse2), "graph-replayed exchange step differs"
         gstep.release()
+        # each decode launched as a programmatic dependent of the previous exchange kernel
+        pstep = atflash.dist.ShardedDecodeStep(step.q, w2, (kc2, vc2), q_pos=q_pos, kv_pos0=kv_pos0,
+                                               out_dtype=torch.float32, exchange=ex, enable_pdl=True)
+        for _ in range(3):
+            op, lp = pstep()
+        torch.cuda.synchronize()
+        assert torch.equal(op, out2) and torch.equal(lp, lse2), "programmatic-launch exchange step differs"
+        pstep.release()
         # the separate-kernel path on the same exchange (decode merge, push,
         # merge): the same bits, and the step protocol carries on between the two
         for _ in range(2):
