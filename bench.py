@@ -1188,9 +1188,12 @@ def main():
         del inputs
         torch.cuda.empty_cache()
         if world == 1:
-            decode = {f"{n // 1024}K": bench_decode(device, 20, 5, peaks, N=n) for n in (8192, 32768, 131072)}
+            # microsecond steps: enough of them (50 warm-up, 200 timed) that the
+            # timed window is not spent while the clocks ramp back up after the
+            # host-side set-up of the leg
+            decode = {f"{n // 1024}K": bench_decode(device, 200, 50, peaks, N=n) for n in (8192, 32768, 131072)}
             decode["reference_kernel_128K"] = bench_reference_decode_kernel(device, peaks)
-        decode_1m = bench_decode_1m(device, rank, world, 20, 5, peaks)
+        decode_1m = bench_decode_1m(device, rank, world, 50, 10, peaks)
         prefill_512k = bench_prefill_512k(device, rank, world, 2, 3, peaks)
     cpu = None
     config1 = None
