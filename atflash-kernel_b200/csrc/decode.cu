@@ -149,6 +149,14 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// D = A(16x8 bf16, row) * B(8x8 bf16, col) + D, fp32 accumulate: one 8-dim
+// slice of a level (the vec8 window reads a level's two slices separately).
+__device__ __forceinline__ void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   uint32_t d;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
@@ -519,8 +527,16 @@ __global__ void __launch_bounds__(THREADS, 2)
   int lim[ATF_MAX_LEVELS];
 #pragma unroll
   for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, q_pos - pos0, i);
-  // ring geometry of this item (the same in every role)
-  const int Lc = k_end > k_beg ? decode::levels_of(lim, k_end - 1) : ATF_MAX_LEVELS;
+  // vec8 (KR only): a key reads level i's first 8-dim slice from lim[i] on (the
+  // level is loaded then) and its second slice from lim2[i] on
+  const bool vec8 = KR && a.window == ATF_WINDOW_VEC8;
+  int lim2[ATF_MAX_LEVELS];
+#pragma unroll
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i)
+    lim2[i] = vec8 ? decode::key_limit(q_pos - pos0, a.zhi8[2 * i + 1]) : lim[i];
+  // ring geometry of this item (the same in every role); at least one level,
+  // since under vec8 not even level 0 need be in window
+  const int Lc = k_end > k_beg ? max(1, decode::levels_of(lim, k_end - 1)) : ATF_MAX_LEVELS;
   const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
   const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
   const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
@@ -556,7 +572,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       int L = 0;
       if (live) {
         const int n_last = min(k0 + r0 + R, k_end) - 1;
-        L = decode::levels_of(lim, n_last);
+        L = max(1, decode::levels_of(lim, n_last));
       }
       // bytes: sum over slices (the K lanes carry them)
       uint32_t my_bytes = (live && !is_v) ? static_cast<uint32_t>(R) * (32u * L + 256u) : 0u;
@@ -634,6 +650,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int last = min(key0 + 15, k_end - 1);
         const int Lmax = decode::levels_of(lim, last);
         const int Lmin = decode::levels_of(lim, key0);
+        // levels both of whose slices every key of the group reads
+        const int Lmin2 = vec8 ? decode::levels_of(lim2, key0) : Lmin;
         // rows past the item end may hold anything (the TMA box covers the
         // whole page slice): zero their V so that P = 0 rows add exactly 0
         if (last < key0 + 15) {
@@ -654,6 +672,8 @@ __global__ void __launch_bounds__(THREADS, 2)
           const bool ok_a = key_a <= last, ok_b = key_b <= last;
           const int La = decode::levels_of(lim, key_a);
           const int Lb = decode::levels_of(lim, key_b);
+          const int La2 = vec8 ? decode::levels_of(lim2, key_a) : La;
+          const int Lb2 = vec8 ? decode::levels_of(lim2, key_b) : Lb;
           float c[4] = {0.f, 0.f, 0.f, 0.f};
           const int lrow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
           const uint32_t krow = static_cast<uint32_t>(lrow * 32 + 16 * ((mi & 1) ^ ((lrow >> 2) & 1)));
@@ -664,9 +684,9 @@ __global__ void __launch_bounds__(THREADS, 2)
               uint32_t m0, m1, m2, m3;
               decode::ldsm_x4(kb + k_slice + i * lstride + krow, m0, m1, m2, m3);
               const uint32_t ak[4] = {m0, m2, m1, m3};
-              if (i < Lmin) {
+              if (i < Lmin2) {
                 decode::mma16816(c, ak, qb[i][0], qb[i][1]);
-              } else {
+              } else if (!vec8) {
                 // level i is active only for the newer keys of the group
                 float t[4] = {0.f, 0.f, 0.f, 0.f};
                 decode::mma16816(t, ak, qb[i][0], qb[i][1]);
@@ -677,6 +697,27 @@ __global__ void __launch_bounds__(THREADS, 2)
                 if (i < Lb) {
                   c[2] += t[2];
                   c[3] += t[3];
+                }
+              } else {
+                // vec8: each 8-dim slice of level i for the keys that read it
+                float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+                decode::mma1688(t0, ak[0], ak[1], qb[i][0]);
+                decode::mma1688(t1, ak[2], ak[3], qb[i][1]);
+                if (i < La) {
+                  c[0] += t0[0];
+                  c[1] += t0[1];
+                }
+                if (i < La2) {
+                  c[0] += t1[0];
+                  c[1] += t1[1];
+                }
+                if (i < Lb) {
+                  c[2] += t0[2];
+                  c[3] += t0[3];
+                }
+                if (i < Lb2) {
+                  c[2] += t1[2];
+                  c[3] += t1[3];
                 }
               }
             }
@@ -1100,9 +1141,15 @@ int atf::decode_launch_split(const AtfDecodeParams* p, cudaStream_t st) {
   int rc = check_device(&dev);
   if (rc != ATF_OK) return rc;
   const int ps = p->page_size;
+  // the TMA kernel reads vec8 windows in its keys-as-rows form (groups of at
+  // most 8 query heads) when the slice table is non-increasing (slices widest
+  // first, as the window tables build it): a key's slices in window are then
+  // a prefix, the first slice of each level no narrower than the second
+  bool vec8_tma = p->num_qo_heads / p->num_kv_heads <= 8;
+  for (int c = 0; c + 1 < ATF_MAX_SLICES; ++c) vec8_tma = vec8_tma && p->zhi8[c] >= p->zhi8[c + 1];
   const bool tma_path = (ps == 16 || ps == 32 || ps == 64 || ps == 128 || ps == 256) &&
-                        p->qk_layout == ATF_LAYOUT_SORTED_PAIR && p->window != ATF_WINDOW_VEC8 &&
-                        p->num_pages >= 1;
+                        p->qk_layout == ATF_LAYOUT_SORTED_PAIR &&
+                        (p->window != ATF_WINDOW_VEC8 || vec8_tma) && p->num_pages >= 1;
   if (p->k_level_major) {
     // only the TMA kernel reads level-major K pages
     if (!tma_path) return ATF_ERR_UNSUPPORTED;

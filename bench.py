@@ -904,6 +904,7 @@ def bench_reference_decode_kernel(device, peaks, N=131072, steps=50, warmup=10):
            "reference_us": {"on_vec8": timeit(lambda: fi(zhi8)), "off": timeit(lambda: fi(None))},
            "ours_us": {"on_snap16": timeit(ours(wt)), "on_vec8": timeit(ours(wt, "vec8")), "off": timeit(ours(None)),
                        "on_snap16_level_major_k": timeit(ours(wt, kk=kc_lm)),
+                       "on_vec8_level_major_k": timeit(ours(wt, "vec8", kk=kc_lm)),
                        "off_level_major_k": timeit(ours(None, kk=kc_lm))}}
     # the two kernels compute the same attention: vec8 window against vec8 window
     ref_on = fi(zhi8)
@@ -916,7 +917,11 @@ def bench_reference_decode_kernel(device, peaks, N=131072, steps=50, warmup=10):
     res["speedup_vs_reference"] = {"on": res["reference_us"]["on_vec8"] / res["ours_us"]["on_snap16"],
                                    "off": res["reference_us"]["off"] / res["ours_us"]["off"],
                                    "on_level_major_k": (res["reference_us"]["on_vec8"]
-                                                        / res["ours_us"]["on_snap16_level_major_k"])}
+                                                        / res["ours_us"]["on_snap16_level_major_k"]),
+                                   # the same window on both sides: vec8 against vec8
+                                   "on_vec8": res["reference_us"]["on_vec8"] / res["ours_us"]["on_vec8"],
+                                   "on_vec8_level_major_k": (res["reference_us"]["on_vec8"]
+                                                             / res["ours_us"]["on_vec8_level_major_k"])}
     byts = WT.decode_bytes(hkv, [N], wt.zhi16)["bytes"]
     res["ours_on_snap16_hbm_frac"] = byts / (res["ours_us"]["on_snap16"] * 1e-6) / 1e9 / peaks["hbm_gbs"]
     del k, v, kc_lm

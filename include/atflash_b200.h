@@ -208,7 +208,9 @@ typedef struct {
   /* Level-major K pages (optional, 0 = k_cache uses the kv strides above):
    * k_cache is [P, Hkv, 8 levels, page, 16] bf16 in sorted-pair order, so the
    * in-window levels of a page are one contiguous run. Needs the sorted-pair
-   * layout, the 16-snap or no window and a page size of 16..256 (power of 2). */
+   * layout, a page size of 16..256 (power of 2) and the 16-snap window, no
+   * window, or a vec8 window with a non-increasing slice table and query-head
+   * groups of at most 8. */
   int k_level_major;
   int64_t k_stride_page, k_stride_head, k_stride_level; /* elements; the token stride is 16 */
   /* Programmatic dependent launch (optional, 0 = off): the split kernel may

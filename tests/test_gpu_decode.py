@@ -159,15 +159,24 @@ def test_decode_window_off_equals_kinf_bitwise(cuda_device):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
-def test_decode_vec8_matches_g2_oracle(cuda_device):
-    """vec8 window (the FlashInfer port's 8-dim slices) vs ref_decode_sliced."""
+@pytest.mark.parametrize("page,level_major,hq,hkv,kv_lens,base", [
+    (16, False, 6, 2, [1000, 2500], 1e4),   # TMA kernel
+    (8, False, 6, 2, [1000, 2500], 1e4),    # cp.async kernel (page 8)
+    (64, True, 28, 4, [20000], 5e5),        # TMA kernel, level-major K, groups of 7
+    (16, False, 48, 4, [3000], 1e4),        # groups of 12: cp.async kernel
+], ids=["tma-p16", "cpasync-p8", "tma-p64-lm-g7", "cpasync-g12"])
+def test_decode_vec8_matches_g2_oracle(cuda_device, page, level_major, hq, hkv, kv_lens, base):
+    """vec8 window (the FlashInfer port's 8-dim slices) vs ref_decode_sliced, on
+    both decode kernels: the TMA kernel splits a level whose second slice only
+    some keys read into two 8-dim MMAs."""
     import atflash
-    kv_lens, hq, hkv = [1000, 2500], 6, 2
-    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, 16, seed=13)
-    wt = atflash.WindowTable(128, 1e4, 2.0)
-    out = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, 16, "NHD", wt, window_mode="vec8")
-    zs = OWT.zhi_slice_vec8(128, 1e4, 2.0)
-    for b in range(2):
+    q, kc, vc, indptr, indices, lpl, ks, vs = make_paged(kv_lens, hq, hkv, page, seed=13)
+    wt = atflash.WindowTable(128, base, 2.0)
+    if level_major:
+        kc = _level_major(kc)
+    out = run_decode(cuda_device, q, kc, vc, indptr, indices, lpl, hq, hkv, page, "NHD", wt, window_mode="vec8")
+    zs = OWT.zhi_slice_vec8(128, base, 2.0)
+    for b in range(len(kv_lens)):
         ref = OA.ref_decode_sliced(q[b].float().numpy(), ks[b].permute(1, 0, 2).float().numpy(),
                                    vs[b].permute(1, 0, 2).float().numpy(), zs, 8)
         mx, mean = err_stats(out[b].float().cpu().numpy(), ref)
