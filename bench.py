@@ -947,12 +947,21 @@ def bench_prefill_512k(device, rank, world, steps, warmup, peaks, N=524288):
         # this rank's zig-zag blocks in one launch (the kernel's row ranges)
         atflash.prefill_fwd(q, k, v, causal=True, window_table=wt, q_offset=0, out=out, row_ranges=live)
     ms, _ = timed(fn, steps, warmup, world)
+    per_rank = timed.per_rank
     work = WT.prefill_work(HQ, N, N, wt.zhi16)
     mine = sum(WT.prefill_work(HQ, e0 - s0, e0, wt.zhi16, q_offset=s0)["flops"] for (s0, e0) in blocks if e0 > s0)
     res = {"ms": ms, "flops_total": work["flops"], "s": work["s"], "ceiling": work["ceiling"],
            "tflops_this_rank": mine / (ms * 1e-3) / 1e12,
            "frac_this_rank": mine / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
            "config": f"N={N}, k=2, zig-zag x{world}, K/V replicated"}
+    if world > 1:
+        # each rank's time and the optional all-gather of the output rows,
+        # timed on its own after the prefill
+        res["ms_per_rank"] = per_rank
+        res["imbalance_max_over_mean"] = max(per_rank) / (sum(per_rank) / len(per_rank))
+        outs = [(s0, e0, out[:, s0:e0]) for (s0, e0) in blocks]
+        ms_g, _ = timed(lambda i: atflash.dist.gather_zigzag(outs, N, world, zhi=wt.zhi16), 2, 3, world)
+        res["gather_zigzag_ms"] = ms_g
     del q, k, v, out
     torch.cuda.empty_cache()
     return res
