@@ -461,7 +461,9 @@ struct KMaps {
 // operand with movmatrix and O^T += V^T P^T takes one MMA per 16 dims. The
 // heads-as-rows form (!KR, any group up to 16) pads the G heads to 16 MMA rows
 // and needs twice the MMAs.
-template <bool KR>
+// VEC8: the vec8 window (KR only), compiled apart so that the 16-snap and
+// window-off instantiations carry none of its per-slice work.
+template <bool KR, bool VEC8>
 __global__ void __launch_bounds__(THREADS, 2)
     decode_tma_kernel(const __grid_constant__ KMaps tmK, const __grid_constant__ CUtensorMap tmV,
                       const Args args) {
@@ -522,25 +524,32 @@ __global__ void __launch_bounds__(THREADS, 2)
   // query, the KV pages) and this kernel's outputs come after the previous
   // grid has completed (immediate without programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
-  const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+  // the query's distance to local key 0, loaded by thread 0 (a consumer) while
+  // the producer warp stages the page list, and shared after the barrier
+  volatile long long* s_zb = reinterpret_cast<volatile long long*>(sp + OFF_BAR + 8 * 2 * NSTAGE_MAX + 8);
+  if (tid == 0) {
+    const long long q_pos = a.q_pos != nullptr ? a.q_pos[b] : kv_len - 1;
+    const long long pos0 = a.kv_pos0 != nullptr ? a.kv_pos0[b] : 0;
+    *s_zb = q_pos - pos0;
+  }
+  __syncthreads();
+  const long long zb = *s_zb;
   int lim[ATF_MAX_LEVELS];
 #pragma unroll
-  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, q_pos - pos0, i);
+  for (int i = 0; i < ATF_MAX_LEVELS; ++i) lim[i] = decode::level_limit(a, zb, i);
   // vec8 (KR only): a key reads level i's first 8-dim slice from lim[i] on (the
   // level is loaded then) and its second slice from lim2[i] on
-  const bool vec8 = KR && a.window == ATF_WINDOW_VEC8;
+  constexpr bool vec8 = KR && VEC8;
   int lim2[ATF_MAX_LEVELS];
 #pragma unroll
   for (int i = 0; i < ATF_MAX_LEVELS; ++i)
-    lim2[i] = vec8 ? decode::key_limit(q_pos - pos0, a.zhi8[2 * i + 1]) : lim[i];
+    lim2[i] = vec8 ? decode::key_limit(zb, a.zhi8[2 * i + 1]) : 0;
   // ring geometry of this item (the same in every role); at least one level,
   // since under vec8 not even level 0 need be in window
   const int Lc = k_end > k_beg ? max(1, decode::levels_of(lim, k_end - 1)) : ATF_MAX_LEVELS;
   const uint32_t K_BYTES = static_cast<uint32_t>(Lc) * KLEVEL_BYTES;
   const uint32_t STAGE_BYTES = K_BYTES + V_BYTES;
   const int NSTAGE = min(NSTAGE_MAX, static_cast<int>(RING_BYTES / STAGE_BYTES));
-  __syncthreads();
   const AbortCtl ab{s_abort, args.err};
   const bool start_ok = (*s_abort == 0);
 
@@ -1226,7 +1235,9 @@ int atf::decode_launch_split(const AtfDecodeParams* p, cudaStream_t st) {
       ta.rows = static_cast<int>(rows);
       ta.err = p->error_flag;
       // groups of at most 8 query heads: keys as the MMA rows
-      auto kern = a.G <= 8 ? decode_tma::decode_tma_kernel<true> : decode_tma::decode_tma_kernel<false>;
+      auto kern = a.G > 8 ? decode_tma::decode_tma_kernel<false, false>
+                  : (p->window == ATF_WINDOW_VEC8 ? decode_tma::decode_tma_kernel<true, true>
+                                                  : decode_tma::decode_tma_kernel<true, false>);
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_tma::SMEM_BYTES) !=
           cudaSuccess)
         return ATF_ERR_CUDA;
