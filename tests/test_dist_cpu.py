@@ -206,3 +206,53 @@ def test_gloo_lost_rank_fails_the_collective_within_the_timeout():
     msg = results.get(0, "hung")
     assert msg.startswith("error after"), msg
     assert float(msg.split()[2].rstrip("s:")) < 60, msg
+
+
+class _FakeWrapper:
+    """Records the keyword arguments of each run() call (host routing only)."""
+
+    def __init__(self):
+        self.calls = []
+
+    def run(self, q, kv, **kw):
+        self.calls.append(kw)
+        B, H, D = q.shape
+        out = torch.zeros((B, H, D), dtype=kw.get("out_dtype") or torch.bfloat16)
+        lse = torch.zeros((B, H), dtype=torch.float32)
+        if kw.get("out") is not None:
+            return kw["out"], kw["lse"]
+        return out, lse
+
+
+class _FakeExchange:
+    def __init__(self, emulated):
+        self._emulated = emulated
+        self.pushed = self.merged = 0
+
+    def push(self, o, lse):
+        self.pushed += 1
+
+    def merge(self, o, lse, out_dtype=torch.bfloat16):
+        self.merged += 1
+        return o.to(out_dtype), lse
+
+
+def test_sharded_decode_routes_exchange_and_programmatic_launch():
+    """One rank, no process group: enable_pdl reaches the decode call; a real
+    exchange runs as the decode's own fused step (exchange= passed to run), an
+    emulated one as the decode followed by separate push and merge."""
+    from atflash import dist as adist
+    q = torch.zeros((1, 4, 128), dtype=torch.bfloat16)
+    pos = torch.tensor([9], dtype=torch.int64)
+    for pdl in (False, True):
+        w = _FakeWrapper()
+        adist.sharded_decode(q, w, (None, None), q_pos=pos, kv_pos0=pos, enable_pdl=pdl)
+        assert w.calls[-1]["enable_pdl"] is pdl and "exchange" not in w.calls[-1]
+        ex = _FakeExchange(emulated=False)
+        adist.sharded_decode(q, w, (None, None), q_pos=pos, kv_pos0=pos, exchange=ex, enable_pdl=pdl)
+        assert w.calls[-1]["exchange"] is ex and w.calls[-1]["enable_pdl"] is pdl
+        assert ex.pushed == 0 and ex.merged == 0
+        ex = _FakeExchange(emulated=True)
+        adist.sharded_decode(q, w, (None, None), q_pos=pos, kv_pos0=pos, exchange=ex, enable_pdl=pdl)
+        assert "exchange" not in w.calls[-1] and w.calls[-1]["out_dtype"] == torch.float32
+        assert ex.pushed == 1 and ex.merged == 1
